@@ -1,0 +1,302 @@
+#!/usr/bin/env python3
+"""Decode throughput of the B200 Q8 path (BASELINE metric: decode tok/s,
+Llama-3.1-8B Q8, 1/2/4/8 B200; Q8 GEMV HBM GB/s vs peak).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--ctx C] [--impl ours|reference]
+
+Workload (config[3]): Llama-3.1-8B architecture, random-init N(0, 0.02) weights
+quantized by the GPU packer (Q8 group 64, f16 scales), KV cache capacity 4096
+per sequence (f32, as the reference), a random prompt prefilled to
+``ctx - warmup - steps`` tokens, then greedy decode of batch B.  A step = one
+decode token for each of the B sequences.  Tensor parallel over N GPUs (one
+process per GPU, NCCL), so per-GPU weight bytes shrink with N ("strong").
+
+* value     : tokens/s with the loop resident on the device (q8_generate: the
+              argmax of each step feeds the next on the GPU), CUDA events on the
+              model stream, barrier + sync on both sides, max over ranks.
+* e2e       : tokens/s through the public per-step API (q8_decode with host
+              ids in pinned staging and the argmax read back every step).
+* roofline  : the Q8 GEMV kernels (dominant): algorithmic bytes (codes + f16
+              scales + activations + outputs) / their CUDA-event durations,
+              from per-launch events of profiled steps after the timed region.
+* cpu_baseline : the CPU port of the reference path (oracle/q8_ref.c, OpenMP,
+              all host threads) timed on a bounded sample of the same decode
+              step (a few full-width layers + the lm_head), scaled by layers.
+* --impl reference : that CPU port alone as the reference arm.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--ctx", type=int, default=4096, help="KV capacity per sequence")
+    ap.add_argument("--model", default="llama-3.1-8b")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU baseline sample")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=32)
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        j = json.load(open(p))
+        return float(j["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if len(s) > 5 + i and s[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------- CPU arm
+def cpu_baseline(cfg, batch: int, ctx: int, layers: int, steps: int = 2):
+    """The CPU port (oracle/q8_ref.c) on a bounded sample of one decode step."""
+    from oracle import q8_ref
+    r = q8_ref.time_decode_sample(cfg, batch=batch, ctx=ctx, sample_layers=layers, steps=steps)
+    return r
+
+
+def run_reference_arm(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from lama32_mojo_b200.config import PRESETS
+    cfg = PRESETS[a.model]
+    ctx = a.ctx - 128
+    r = cpu_baseline(cfg, a.batch, ctx, a.cpu_layers, steps=max(1, min(a.steps, 3)))
+    line = {
+        "impl": "reference", "metric": "decode tok/s", "value": r["tok_s"], "unit": "tok/s",
+        "n_gpus": a.gpus, "steps": r["steps"], "warmup": 1, "ms_per_step": r["ms_per_step"],
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": f"{a.model} Q8 decode batch {a.batch} at ctx {ctx}",
+                                        "model": a.model, "global_batch": a.batch, "seq_len": ctx},
+        "cpu_baseline": {"value": r["tok_s"], "unit": "tok/s", "cores": r["threads"], "kind": "port",
+                         "sample": r["sample"]},
+        "e2e": {"value": r["tok_s"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def main():
+    a = parse()
+    if a.impl == "reference":
+        return run_reference_arm(a)
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from lama32_mojo_b200.config import PRESETS
+    from lama32_mojo_b200.model import Q8Model, load_synthetic, nccl_unique_id
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != a.gpus:
+        raise SystemExit(f"--gpus {a.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=300))
+        uid = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        nid = uid[0]
+    else:
+        nid = None
+
+    cfg = PRESETS[a.model]
+    B = a.batch
+    prompt = a.ctx - a.warmup - a.steps - a.e2e_steps - 8
+    assert prompt > 0, "ctx too small for warmup+steps"
+    m = load_synthetic(cfg, device=local, seed=0, maxlen=a.ctx, max_seqs=B, max_tokens=2048,
+                       tp_rank=rank, tp_size=world, nccl_id=nid)
+    rng = np.random.default_rng(1)
+    first = []
+    for b in range(B):
+        ids = rng.integers(0, cfg.vocab, size=prompt).tolist()
+        first.append(m.forward_argmax(ids, seq=b))
+    seqs = list(range(B))
+    ext = torch.cuda.ExternalStream(m.stream, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # warmup (graph capture + clocks)
+    toks = m.generate(first, seqs, a.warmup)
+    cur = toks[-1].tolist()
+
+    # ---- timed region: value (device-resident greedy loop)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(ext)
+        toks = m.generate(cur, seqs, a.steps)
+        e1.record(ext)
+        torch.cuda.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    cur = toks[-1].tolist()
+    ms_per_step = ms / a.steps
+    value = B * a.steps / (ms / 1e3)
+
+    # ---- e2e: per-step public API, host ids in, host argmax out
+    barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(ext)
+    for _ in range(a.e2e_steps):
+        cur = m.decode(cur, seqs).tolist()
+    f1.record(ext)
+    torch.cuda.synchronize()
+    barrier()
+    ems = f0.elapsed_time(f1)
+    if world > 1:
+        t = torch.tensor([ems], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ems = float(t.item())
+    e2e = B * a.e2e_steps / (ems / 1e3)
+
+    # ---- roofline of the dominant kernel (Q8 GEMV), per-launch CUDA events
+    m.set_profiling(True)
+    agg = {}
+    nprof = 4
+    for _ in range(nprof):
+        cur = m.decode(cur, seqs).tolist()
+        for k, (kms, kb, kl) in m.profile().items():
+            s = agg.setdefault(k, [0.0, 0.0, 0])
+            s[0] += kms
+            s[1] += kb
+            s[2] += kl
+    m.set_profiling(False)
+    gemv = [k for k in agg if k.startswith("gemv_")]
+    g_ms = sum(agg[k][0] for k in gemv)
+    g_b = sum(agg[k][1] for k in gemv)
+    g_l = sum(agg[k][2] for k in gemv)
+    peak, peak_kind = load_peaks()
+    achieved = g_b / (g_ms / 1e3) / 1e9 if g_ms > 0 else 0.0
+    step_ms_prof = sum(v[0] for v in agg.values()) / nprof
+    breakdown = {k: {"ms_per_step": round(v[0] / nprof, 4), "launches_per_step": v[2] // nprof,
+                     "GB_s": round(v[1] / (v[0] / 1e3) / 1e9, 1) if v[0] > 0 else None} for k, v in agg.items()}
+    traffic = None
+    tp = os.path.join(REPO, "profiles", "gemv_traffic.json")
+    if os.path.exists(tp):
+        tj = json.load(open(tp))
+        traffic = tj.get(f"{a.model}/tp{world}/b{B}")
+
+    # launches per step: our kernels inside the graph
+    launches_per_step = sum(v[2] for v in agg.values()) // nprof
+    gpu_launches = launches_per_step * a.steps
+
+    ctx_mid = prompt + a.warmup + a.steps // 2
+    step_bytes = cfg.decode_bytes(B, ctx_mid, tp=world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu:
+        try:
+            r = cpu_baseline(cfg, B, ctx_mid, a.cpu_layers)
+            cpu = {"value": r["tok_s"], "unit": "tok/s", "cores": r["threads"], "kind": "port",
+                   "sample": r["sample"]}
+        except Exception as ex:  # the GPU number stands without it
+            cpu = {"value": None, "unit": "tok/s", "cores": None, "kind": "port", "sample": f"failed: {ex}"}
+
+    if rank == 0:
+        line = {
+            "metric": "decode tok/s", "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8xf32",
+            "data": "synthetic (random-init N(0,0.02) weights, random prompt ids)",
+            "config": {"workload": f"{a.model} Q8 greedy decode, batch {B}, KV capacity {a.ctx}, "
+                                   f"context {prompt}..{prompt + a.warmup + a.steps + a.e2e_steps + nprof}",
+                       "model": a.model, "global_batch": B, "seq_len": a.ctx, "prompt": prompt,
+                       "parallelism": f"tp{world}", "kv_dtype": "f32",
+                       "l2": "weights+KV per step > 126 MB L2 (no flush needed)"},
+            "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 12 * B,
+                    "d2h_bytes_per_step": 4 * B},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "kernel": "k_gemv_q8 (all Q8 GEMV launches of a decode step)",
+                         "peak_source": f"{peak_kind} hbm_gbs", "launches_per_step": g_l // nprof},
+            "step_roofline": {"bytes_per_step": step_bytes, "achieved_GB_s": round(step_bytes / (ms_per_step / 1e3) / 1e9, 1),
+                              "frac": round(step_bytes / (ms_per_step / 1e3) / 1e9 / peak, 4)},
+            "kernels": breakdown, "profiled_step_ms": round(step_ms_prof, 4),
+            "gpu_launches": gpu_launches, "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    m.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,52 @@
+// Internal launcher declarations shared by the op-level ABI and the model runtime.
+#pragma once
+#include "q8_common.cuh"
+
+namespace q8 {
+
+enum { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
+
+int pack_launch(const void* w_bf16, int64_t n, int64_t m, void* packed, cudaStream_t st);
+int to_xs_launch(const void* x, int dtype, int64_t ldx, int M, int K, __half* xs, cudaStream_t st);
+int gemv_launch(int epi, const __half* xs, int M, int K, const void* W, int N, float* y,
+                int64_t ldy, __half* ys, cudaStream_t st);
+// Chooses the small-M tensor-core GEMV or the tcgen05 tile GEMM by M.
+int gemm_dispatch(int epi, const __half* xs, int M, int K, const void* W, int N, float* y,
+                  int64_t ldy, __half* ys, cudaStream_t st);
+int op_scratch(size_t bytes, void** out);
+
+int embed_launch(const void* packed_emb, int64_t d, const int32_t* ids, int64_t s, float* y,
+                 cudaStream_t st);
+// y32 / yxs may be null; resid may be null.
+int rmsnorm_launch(float* x, const float* resid, const uint16_t* w, int64_t rows, int64_t d,
+                   float eps, float* y32, __half* yxs, cudaStream_t st);
+int rmsnorm_heads_launch(const float* x, const uint16_t* w, int64_t rows, int64_t hd, float eps,
+                         float* y, cudaStream_t st);
+int rope_kv_launch(float* qkv, int64_t ldqkv, int64_t T, const int32_t* pos, const int32_t* seq,
+                   int nh, int nkv, int hd, const float* inv_freq, const uint16_t* qn,
+                   const uint16_t* kn, float eps, float* kp, float* vp, int page,
+                   const int32_t* bt, int max_pages, cudaStream_t st);
+
+struct AttnArgs {
+  const float* q; int64_t ldq;
+  int T;
+  const int32_t* pos; const int32_t* seq;
+  int nh, nkv, hd;
+  const float* kp; const float* vp; int page;
+  const int32_t* bt; int max_pages;
+  // query blocks: token range [qb_tok0[i], qb_tok0[i]+qb_len[i]) of one sequence
+  // with consecutive positions; null => one block per token.
+  const int32_t* qb_tok0; const int32_t* qb_len; int nqb; int qb_max;
+  int nsplit;
+  float* part;                 // scratch: nqb*nkv*nsplit*(rmax*hd + 2*rmax) floats
+  float* out32; int64_t ldo;   // nullable
+  __half* outxs;               // nullable, XS over K = nh*hd
+};
+int attention_init();
+int attention_launch(const AttnArgs& a, cudaStream_t st);
+size_t attention_part_floats(int nqb, int nkv, int nsplit, int qb_max, int group, int hd);
+
+int argmax_launch(const float* logits, int64_t rows, int64_t n, int64_t ld, int32_t* out,
+                  cudaStream_t st);
+
+}  // namespace q8
