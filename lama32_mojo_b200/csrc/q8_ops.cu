@@ -375,10 +375,10 @@ int attention_init() {
   int dev = 0;
   Q8_CUDA(cudaGetDevice(&dev));
   if (done[dev & 63]) return Q8_OK;
-  Q8_TRY(attn_set_smem<64, 8>());
-  Q8_TRY(attn_set_smem<64, 64>());
-  Q8_TRY(attn_set_smem<128, 8>());
-  Q8_TRY(attn_set_smem<128, 64>());
+  Q8_TRY((attn_set_smem<64, 8>()));
+  Q8_TRY((attn_set_smem<64, 64>()));
+  Q8_TRY((attn_set_smem<128, 8>()));
+  Q8_TRY((attn_set_smem<128, 64>()));
   done[dev & 63] = true;
   return Q8_OK;
 }
