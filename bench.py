@@ -193,10 +193,12 @@ def main():
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        torch.cuda.nvtx.range_push("decode_timed")
         e0.record(ext)
         toks = m.generate(cur, seqs, a.steps)
         e1.record(ext)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     barrier()
     ms = e0.elapsed_time(e1)
     if world > 1:

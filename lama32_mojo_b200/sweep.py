@@ -1,0 +1,87 @@
+"""Q8 GEMV/GEMM kernel sweep (benchmark config[1]).
+
+    python -m lama32_mojo_b200.sweep [--shapes 1b,3b] [--m 1,8,64,512,4096] [--one K,N,M] [--iters 20]
+
+Every projection shape of Llama-3.2-1B / 3B (K x N), int8 weights from N(0, 0.02)
+with group-64 f16 scales packed by the GPU packer, bf16 activations N(0, 1),
+M tokens.  Each case times ``q8op_gemm`` with CUDA events on the current stream
+after warm-up, rotating over enough weight copies that every launch reads
+weights from HBM (> 126 MB L2 per rotation), and prints one JSON line with the
+achieved HBM GB/s (algorithmic bytes: codes + scales + activations + output)
+and TFLOP/s (2*M*N*K).  ``--one`` runs a single case (the small command used
+for ncu captures).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+SHAPES = {
+    "1b": [(2048, 3072), (2048, 2048), (2048, 512), (2048, 16384), (2048, 8192), (8192, 2048)],
+    "3b": [(3072, 5120), (3072, 3072), (3072, 1024), (3072, 16384), (3072, 8192), (8192, 3072)],
+}
+
+
+def peaks():
+    p = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        j = json.load(open(p))
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def run_case(K, N, M, iters=20, warmup=5):
+    import torch
+    from . import ops
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(K * 7 + N)
+    wbytes = N * (K + K // 32)
+    copies = max(1, -(-300 * 2 ** 20 // wbytes))  # > 2x L2 per rotation
+    copies = min(copies, 64)
+    ws = [ops.pack_q8((torch.randn((N, K), generator=g, device=dev) * 0.02).to(torch.bfloat16))
+          for _ in range(copies)]
+    x = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+    y = torch.empty((M, N), device=dev)
+    for i in range(warmup):
+        ops.mm_q8(x, ws[i % copies], K, out=y)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(iters):
+        ops.mm_q8(x, ws[i % copies], K, out=y)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    bytes_ = wbytes + M * K * 2 + M * N * 4
+    return {"K": K, "N": N, "M": M, "us": round(ms * 1e3, 2), "GB_s": round(bytes_ / (ms / 1e3) / 1e9, 1),
+            "TFLOP_s": round(2.0 * M * N * K / (ms / 1e3) / 1e12, 2)}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--shapes", default="1b,3b")
+    ap.add_argument("--m", default="1,8,64,512,4096")
+    ap.add_argument("--one", default=None, help="K,N,M")
+    ap.add_argument("--iters", type=int, default=20)
+    a = ap.parse_args()
+    hbm, tc, kind = peaks()
+    if a.one:
+        K, N, M = (int(v) for v in a.one.split(","))
+        cases = [(K, N, M)]
+    else:
+        cases = [(K, N, M) for s in a.shapes.split(",") for (K, N) in SHAPES[s]
+                 for M in (int(v) for v in a.m.split(","))]
+    for K, N, M in cases:
+        r = run_case(K, N, M, iters=a.iters)
+        bound = "hbm" if 2 * M < 140 else "tensor"
+        r["bound"] = bound
+        r["frac"] = round(r["GB_s"] / hbm, 4) if bound == "hbm" else round(r["TFLOP_s"] / tc, 4)
+        r["peak_source"] = kind
+        print(json.dumps(r), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
