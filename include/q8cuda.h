@@ -91,6 +91,23 @@ int q8op_dequant(const void* packed, int64_t n, int64_t m, float* w, void* strea
 int q8op_gemm(const void* x, int x_dtype, int64_t ldx, int64_t M, int64_t K,
               const void* packed_w, int64_t N, float* y, int64_t ldy, void* stream);
 
+/* Allocation-free variant of q8op_gemm (no counterpart in the reference).
+ * Some callers cannot call cudaMalloc: a host that owns a fixed device-memory
+ * budget handed out by its own pool (a Mojo DeviceContext arena, an inference
+ * server that reserves all memory at start-up), or code on a path where an
+ * allocation's implicit device synchronization or failure is not acceptable.
+ * This entry point stages x in a file-scope __device__ array of
+ * Q8_NOALLOC_MAX_ELEMS split-f16 elements (8 MiB, held by every GPU that loads
+ * the library until the process exits) instead of a cudaMalloc'd buffer.
+ * It rejects M*K > Q8_NOALLOC_MAX_ELEMS with Q8_ERR_ARG.  The array's device
+ * address is looked up on the first call on each device (that call should come
+ * before any stream capture on the device).  Every call shares the array:
+ * calls whose executions overlap on the GPU (other streams, other threads)
+ * race; serialize them.  Caller still owns x and y. */
+#define Q8_NOALLOC_MAX_ELEMS (2 * 1024 * 1024)
+int q8op_gemm_noalloc(const void* x, int x_dtype, int64_t ldx, int64_t M, int64_t K,
+                      const void* packed_w, int64_t N, float* y, int64_t ldy, void* stream);
+
 /* Fused gate|up GEMV + SwiGLU: act[M, F] = silu(x.Wg^T) * (x.Wu^T) where
  * packed_gu holds the F gate rows followed by the F up rows — replaces the
  * s==1 fused gate|up mm_q8_op + k_swiglu_mul (src/llama_q8.mojo:215-224,

@@ -52,6 +52,7 @@ SIGNATURES = {
     "q8op_pack": [_P, _I64, _I64, _P, _P],
     "q8op_dequant": [_P, _I64, _I64, _P, _P],
     "q8op_gemm": [_P, _I32, _I64, _I64, _I64, _P, _I64, _P, _I64, _P],
+    "q8op_gemm_noalloc": [_P, _I32, _I64, _I64, _I64, _P, _I64, _P, _I64, _P],
     "q8op_gemm_swiglu": [_P, _I32, _I64, _I64, _I64, _P, _I64, _P, _I64, _P],
     "q8op_embed": [_P, _I64, _I64, _P, _I64, _P, _P],
     "q8op_rmsnorm": [_P, _P, _P, _I64, _I64, _F, _P, _P],

@@ -22,6 +22,7 @@
 //    (k_swiglu_mul, src/llama_common.mojo:476-481), written as XS for down.
 #include "q8_kernels.h"
 #include <algorithm>
+#include <mutex>
 
 namespace q8 {
 
@@ -315,4 +316,52 @@ extern "C" int q8op_gemm_swiglu(const void* x, int x_dtype, int64_t ldx, int64_t
                                 const void* packed_gu, int64_t F, float* act, int64_t ld_act,
                                 void* stream) {
   return op_gemm_common(EPI_SWIGLU, x, x_dtype, ldx, M, K, packed_gu, F, act, ld_act, stream);
+}
+
+// ---------------------------------------------------------------- allocation-free entry
+// Staging for q8op_gemm_noalloc: x converted to split-f16 (2 halves per
+// element).  A file-scope device array, so the entry point never allocates.
+static __device__ __align__(256) __half g_noalloc_xs[2 * Q8_NOALLOC_MAX_ELEMS];
+
+namespace q8 {
+// Device address of g_noalloc_xs per device.  In host code the symbol is only
+// a host-side shadow; the device address comes from cudaGetSymbolAddress,
+// resolved once per device with that device current.
+static __half* g_noalloc_dev[64];
+static std::mutex g_noalloc_mu;
+
+static int noalloc_staging(__half** out) {
+  int dev = 0;
+  Q8_CUDA(cudaGetDevice(&dev));
+  Q8_CHECK_ARG(dev >= 0 && dev < 64, "q8op_gemm_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_dev[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_xs);
+    if (e != cudaSuccess || !p) {
+      set_error("q8op_gemm_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      return Q8_ERR_CUDA;
+    }
+    g_noalloc_dev[dev] = (__half*)p;
+  }
+  *out = g_noalloc_dev[dev];
+  return Q8_OK;
+}
+}  // namespace q8
+
+extern "C" int q8op_gemm_noalloc(const void* x, int x_dtype, int64_t ldx, int64_t M, int64_t K,
+                                 const void* packed_w, int64_t N, float* y, int64_t ldy, void* stream) {
+  Q8_CHECK_ARG(x && packed_w && y, "q8op_gemm_noalloc: null pointer");
+  Q8_CHECK_ARG(x_dtype == Q8_F32 || x_dtype == Q8_BF16 || x_dtype == Q8_F16, "q8op_gemm_noalloc: bad x_dtype");
+  Q8_CHECK_ARG(M > 0 && K > 0 && N > 0 && K % Q8_QG == 0 && ldx >= K && ldy >= N, "q8op_gemm_noalloc: bad shape");
+  Q8_CHECK_ARG(N < (1 << 30), "q8op_gemm_noalloc: N too large");
+  Q8_CHECK_ARG(M * K <= (int64_t)Q8_NOALLOC_MAX_ELEMS,
+               "q8op_gemm_noalloc: M*K = %lld exceeds the static staging capacity of %d elements",
+               (long long)(M * K), (int)Q8_NOALLOC_MAX_ELEMS);
+  cudaStream_t st = (cudaStream_t)stream;
+  __half* xs = nullptr;
+  Q8_TRY(noalloc_staging(&xs));
+  // every staged element is written before it is read: nothing to clear
+  Q8_TRY(to_xs_launch(x, x_dtype, ldx, (int)M, (int)K, xs, st));
+  return gemm_dispatch(EPI_STORE, xs, (int)M, (int)K, packed_w, (int)N, y, ldy, nullptr, st);
 }

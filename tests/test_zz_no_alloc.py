@@ -1,0 +1,57 @@
+"""The allocation-free GEMM entry point, called through the C ABI.
+
+Callers that cannot allocate device memory (a host with its own fixed device
+memory pool, or code that must not trigger cudaMalloc's implicit
+synchronization) use q8op_gemm_noalloc, which stages activations in a static
+device array instead of a cudaMalloc'd buffer.  Its output must match
+q8op_gemm on two calls in a row (the second call reuses the static array the
+first one left behind).  This file is collected last on purpose.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+from lama32_mojo_b200 import _lib, ops
+from oracle import q8_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+MAX_ELEMS = 2 * 1024 * 1024  # Q8_NOALLOC_MAX_ELEMS in include/q8cuda.h
+
+
+def _call(fn, x, packed, K, y):
+    s = torch.cuda.current_stream().cuda_stream
+    return fn(C.c_void_p(x.data_ptr()), _lib.Q8_F32, x.stride(0), x.shape[0], K, C.c_void_p(packed.data_ptr()),
+              packed.shape[0], C.c_void_p(y.data_ptr()), y.stride(0), C.c_void_p(s))
+
+
+def test_noalloc_gemm_matches_gemm_twice(cuda):
+    L = _lib.lib()
+    g = torch.Generator(device=cuda).manual_seed(123)
+    cases = [(1, 4096, 6144), (8, 14336, 4096)]  # decode shapes of Llama-3.1-8B
+    for M, K, N in cases:
+        w = (torch.randn((N, K), generator=g, device=cuda) * 0.02).to(torch.bfloat16)
+        p = ops.pack_q8(w)
+        x = torch.randn((M, K), generator=g, device=cuda)
+        y_ref = torch.empty((M, N), device=cuda)
+        y_new = torch.full((M, N), float("nan"), device=cuda)
+        _lib.check(_call(L.q8op_gemm, x, p, K, y_ref))
+        _lib.check(_call(L.q8op_gemm_noalloc, x, p, K, y_new))
+        torch.cuda.synchronize()
+        a, b = y_new.cpu().numpy(), y_ref.cpu().numpy()
+        assert np.isfinite(a).all()
+        assert O.rel_l2(a, b) <= 1e-5 and np.abs(a - b).max() <= 1e-4, (M, K, N)
+
+
+def test_noalloc_gemm_rejects_oversize(cuda):
+    L = _lib.lib()
+    K = 4096
+    M = MAX_ELEMS // K + 1
+    x = torch.zeros((M, K), device=cuda)
+    p = torch.zeros((16, K // 64 + K // 2), dtype=torch.int16, device=cuda)
+    y = torch.zeros((M, 16), device=cuda)
+    st = _call(L.q8op_gemm_noalloc, x, p, K, y)
+    assert st == _lib.Q8_ERR_ARG
+    assert "static staging capacity" in _lib.last_error()
