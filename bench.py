@@ -19,7 +19,7 @@ process per GPU, NCCL), so per-GPU weight bytes shrink with N ("strong").
 * roofline  : the Q8 GEMV kernels (dominant): algorithmic bytes (codes + f16
               scales + activations + outputs) / their CUDA-event durations,
               from per-launch events of profiled steps after the timed region.
-* cpu_baseline : the CPU port of the reference path (oracle/q8_ref.c, OpenMP,
+* cpu_baseline : the CPU port of the reference path (oracle/q8_ref.c, pthreads,
               all host threads) timed on a bounded sample of the same decode
               step (a few full-width layers + the lm_head), scaled by layers.
 * --impl reference : that CPU port alone as the reference arm.

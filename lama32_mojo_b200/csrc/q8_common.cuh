@@ -92,6 +92,97 @@ __device__ __forceinline__ float warp_max(float v) {
 
 inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
 
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream-serialization attribute may start while its predecessor in the
+// stream is still running; it must call pdl_wait() before touching anything
+// the predecessor writes (weights and other read-only inputs may be read
+// before).  pdl_trigger() lets the successor launch early.  Both are no-ops
+// for ordinary launches.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---- shared-memory barriers + bulk async copies (TMA engine, no tensor map)
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// make barrier initialization visible to the async (TMA) proxy
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Device-side error word (one per translation unit): a bounded wait that
+// gives up records its code here.
+static __device__ int g_q8_device_error;
+
+// Bounded wait on a barrier phase: gives up after ~2^31 cycles (about a
+// second), records Q8_ERR_TIMEOUT in g_q8_device_error and returns false, so
+// a lost completion never hangs the GPU.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > (1ll << 31)) {
+      atomicExch(&g_q8_device_error, Q8_ERR_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
+// 1-D bulk copy global -> this CTA's shared memory; completion counts bytes on bar.
+// src, dst 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Whether decode-path launches use programmatic dependent launch (env Q8_PDL=0 disables).
+bool pdl_enabled();
+
+// cudaLaunchKernelEx with the programmatic stream-serialization attribute.
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                      cudaStream_t st, Args... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+  if (e != cudaSuccess) {
+    set_error("launch %s: %s", what, cudaGetErrorString(e));
+    return Q8_ERR_CUDA;
+  }
+  return Q8_OK;
+}
+
 int num_sms();
 
 }  // namespace q8

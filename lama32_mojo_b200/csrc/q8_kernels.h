@@ -8,11 +8,17 @@ enum { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
 
 int pack_launch(const void* w_bf16, int64_t n, int64_t m, void* packed, cudaStream_t st);
 int to_xs_launch(const void* x, int dtype, int64_t ldx, int M, int K, __half* xs, cudaStream_t st);
-int gemv_launch(int epi, const __half* xs, int M, int K, const void* W, int N, float* y,
-                int64_t ldy, __half* ys, cudaStream_t st);
-// Chooses the small-M tensor-core GEMV or the tcgen05 tile GEMM by M.
-int gemm_dispatch(int epi, const __half* xs, int M, int K, const void* W, int N, float* y,
-                  int64_t ldy, __half* ys, cudaStream_t st);
+int gemv_init();
+int gemv_rms_launch(int epi, const float* h, int64_t ldh, const uint16_t* nw, float eps, int M, int K,
+                    const void* W, int N, float* y, int64_t ldy, __half* ys, cudaStream_t st);
+// Activations come as f32 rows (x32, used by the int8-digit kernel) and/or the
+// split-f16 XS rows (xs, used by the general kernel); either may be null when
+// the other covers the shape.
+int gemv_launch(int epi, const float* x32, int64_t ldx32, const __half* xs, int M, int K, const void* W, int N,
+                float* y, int64_t ldy, __half* ys, cudaStream_t st);
+// Chooses the decode GEMV kernels or (later) the tensor-core tile GEMM by M.
+int gemm_dispatch(int epi, const float* x32, int64_t ldx32, const __half* xs, int M, int K, const void* W, int N,
+                  float* y, int64_t ldy, __half* ys, cudaStream_t st);
 int op_scratch(size_t bytes, void** out);
 
 int embed_launch(const void* packed_emb, int64_t d, const int32_t* ids, int64_t s, float* y,
@@ -45,6 +51,12 @@ struct AttnArgs {
 int attention_init();
 int attention_launch(const AttnArgs& a, cudaStream_t st);
 size_t attention_part_floats(int nqb, int nkv, int nsplit, int qb_max, int group, int hd);
+
+size_t attention_decode_part_floats(int T, int nkv, int nsplit, int group, int hd);
+int attention_decode_launch(const float* q, int64_t ldq, int T, const int32_t* pos, const int32_t* seq, int nh,
+                            int nkv, int hd, const float* kp, const float* vp, int page, const int32_t* bt,
+                            int max_pages, int nsplit, float* part, int* ticket, float* out32, int64_t ldo,
+                            __half* outxs, cudaStream_t st);
 
 int argmax_launch(const float* logits, int64_t rows, int64_t n, int64_t ld, int32_t* out,
                   cudaStream_t st);

@@ -38,6 +38,15 @@ void set_error(const char* fmt, ...) {
 }
 const char* get_error() { return t_err.c_str(); }
 
+bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("Q8_PDL");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 int num_sms() {
   static int cache[64] = {0};
   int dev = 0;
@@ -163,11 +172,13 @@ struct q8_ctx {
 
   int32_t *ids_d = nullptr, *pos_d = nullptr, *seq_d = nullptr, *qb_tok0_d = nullptr, *qb_len_d = nullptr;
   int32_t *argmax_d = nullptr, *hist_d = nullptr, *ctr_d = nullptr;
+  int* ticket_d = nullptr;  // attention split tickets, zero at rest
   int hist_cap = 0;
   int32_t* pin = nullptr;  // pinned staging: 5 * max_tokens int32
   float *h = nullptr, *qkv = nullptr, *ypart = nullptr, *logits = nullptr, *part = nullptr;
   size_t part_floats = 0;
   __half *xs_in = nullptr, *xs_ao = nullptr, *xs_act = nullptr;
+  float *xn32 = nullptr, *ao32 = nullptr, *act32 = nullptr;  // f32 copies of the GEMV inputs
   float *am_val = nullptr, *am_gval = nullptr, *lg_gather = nullptr;
   int32_t *am_idx = nullptr, *am_gidx = nullptr;
   float* logits_host_pin = nullptr;
@@ -242,12 +253,20 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
   PROF(c, "embed", (double)T * (q8_row_bytes(H) + H * 4.0),
        embed_launch(c->embed, H, c->ids_d, T, c->h, st));
   const float* pending = nullptr;  // row-parallel partial sum not yet added to h
+  // small token batches fuse RMSNorm into the GEMV prologue (K = hidden fits
+  // the shared-memory staging); large batches keep the standalone kernel
+  const bool fuse_norm = H <= 6144 && T <= 64;
   for (int L = 0; L < c->cfg.layers; ++L) {
     const LayerW& w = c->layers[L];
-    PROF(c, "rmsnorm", (double)T * H * (pending ? 16.0 : 8.0),
-         rmsnorm_launch(c->h, pending, w.in_norm, T, H, c->cfg.eps, nullptr, c->xs_in, st));
-    PROF(c, "gemv_qkv", gemv_bytes(T, H, nqkv),
-         gemm_dispatch(EPI_STORE, c->xs_in, T, H, w.qkv, nqkv, c->qkv, nqkv, nullptr, st));
+    if (!pending && fuse_norm) {  // RMSNorm fused into the GEMV prologue
+      PROF(c, "gemv_qkv", gemv_bytes(T, H, nqkv),
+           gemv_rms_launch(EPI_STORE, c->h, H, w.in_norm, c->cfg.eps, T, H, w.qkv, nqkv, c->qkv, nqkv, nullptr, st));
+    } else {
+      PROF(c, "rmsnorm", (double)T * H * (pending ? 16.0 : 8.0),
+           rmsnorm_launch(c->h, pending, w.in_norm, T, H, c->cfg.eps, c->xn32, c->xs_in, st));
+      PROF(c, "gemv_qkv", gemv_bytes(T, H, nqkv),
+           gemm_dispatch(EPI_STORE, c->xn32, H, c->xs_in, T, H, w.qkv, nqkv, c->qkv, nqkv, nullptr, st));
+    }
     PROF(c, "rope_kv", (double)T * (c->qd + 3.0 * c->kvd) * 8.0,
          rope_kv_launch(c->qkv, nqkv, T, c->pos_d, c->seq_d, c->nh, c->nkv, c->hd, c->inv_freq_d, w.q_norm,
                         w.k_norm, c->cfg.eps, c->kpool + (size_t)L * c->layer_kv,
@@ -259,28 +278,41 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
     a.page = c->page; a.bt = c->bt_d; a.max_pages = c->max_pages;
     a.qb_tok0 = blocks ? c->qb_tok0_d : nullptr; a.qb_len = blocks ? c->qb_len_d : nullptr;
     a.nqb = nqb; a.qb_max = qb_max; a.nsplit = nsplit; a.part = c->part;
-    a.out32 = nullptr; a.ldo = 0; a.outxs = c->xs_ao;
-    PROF(c, "attention", kv_bytes_hint / c->cfg.layers + (double)T * c->qd * 8.0, attention_launch(a, st));
+    a.out32 = c->ao32; a.ldo = c->qd; a.outxs = c->xs_ao;
+    if (blocks) {
+      PROF(c, "attention", kv_bytes_hint / c->cfg.layers + (double)T * c->qd * 8.0, attention_launch(a, st));
+    } else {
+      PROF(c, "attention", kv_bytes_hint / c->cfg.layers + (double)T * c->qd * 8.0,
+           attention_decode_launch(c->qkv, nqkv, T, c->pos_d, c->seq_d, c->nh, c->nkv, c->hd, a.kp, a.vp, c->page,
+                                   c->bt_d, c->max_pages, nsplit, c->part, c->ticket_d, c->ao32, c->qd,
+                                   c->xs_ao, st));
+    }
     if (!tp) {
       PROF(c, "gemv_o", gemv_bytes(T, c->qd, H),
-           gemm_dispatch(EPI_ADD, c->xs_ao, T, c->qd, w.o, H, c->h, H, nullptr, st));
+           gemm_dispatch(EPI_ADD, c->ao32, c->qd, c->xs_ao, T, c->qd, w.o, H, c->h, H, nullptr, st));
     } else {
       PROF(c, "gemv_o", gemv_bytes(T, c->qd, H),
-           gemm_dispatch(EPI_STORE, c->xs_ao, T, c->qd, w.o, H, c->ypart, H, nullptr, st));
+           gemm_dispatch(EPI_STORE, c->ao32, c->qd, c->xs_ao, T, c->qd, w.o, H, c->ypart, H, nullptr, st));
       PROF(c, "allreduce", (double)T * H * 4.0, allreduce(c, c->ypart, (size_t)T * H));
       pending = c->ypart;
     }
-    PROF(c, "rmsnorm", (double)T * H * (pending ? 16.0 : 8.0),
-         rmsnorm_launch(c->h, pending, w.post_norm, T, H, c->cfg.eps, nullptr, c->xs_in, st));
+    if (!pending && fuse_norm) {
+      PROF(c, "gemv_gateup", gemv_bytes(T, H, 2 * c->F),
+           gemv_rms_launch(EPI_SWIGLU, c->h, H, w.post_norm, c->cfg.eps, T, H, w.gu, c->F, c->act32, c->F,
+                           c->xs_act, st));
+    } else {
+      PROF(c, "rmsnorm", (double)T * H * (pending ? 16.0 : 8.0),
+           rmsnorm_launch(c->h, pending, w.post_norm, T, H, c->cfg.eps, c->xn32, c->xs_in, st));
+      PROF(c, "gemv_gateup", gemv_bytes(T, H, 2 * c->F),
+           gemm_dispatch(EPI_SWIGLU, c->xn32, H, c->xs_in, T, H, w.gu, c->F, c->act32, c->F, c->xs_act, st));
+    }
     pending = nullptr;
-    PROF(c, "gemv_gateup", gemv_bytes(T, H, 2 * c->F),
-         gemm_dispatch(EPI_SWIGLU, c->xs_in, T, H, w.gu, c->F, nullptr, 0, c->xs_act, st));
     if (!tp) {
       PROF(c, "gemv_down", gemv_bytes(T, c->F, H),
-           gemm_dispatch(EPI_ADD, c->xs_act, T, c->F, w.down, H, c->h, H, nullptr, st));
+           gemm_dispatch(EPI_ADD, c->act32, c->F, c->xs_act, T, c->F, w.down, H, c->h, H, nullptr, st));
     } else {
       PROF(c, "gemv_down", gemv_bytes(T, c->F, H),
-           gemm_dispatch(EPI_STORE, c->xs_act, T, c->F, w.down, H, c->ypart, H, nullptr, st));
+           gemm_dispatch(EPI_STORE, c->act32, c->F, c->xs_act, T, c->F, w.down, H, c->ypart, H, nullptr, st));
       PROF(c, "allreduce", (double)T * H * 4.0, allreduce(c, c->ypart, (size_t)T * H));
       pending = c->ypart;
     }
@@ -288,10 +320,17 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
   if (lrows <= 0) return Q8_OK;
   float* hrow = c->h + (size_t)lrow0 * H;
   const float* prow = pending ? pending + (size_t)lrow0 * H : nullptr;
-  PROF(c, "rmsnorm", (double)lrows * H * 8.0,
-       rmsnorm_launch(hrow, prow, c->final_norm, lrows, H, c->cfg.eps, nullptr, c->xs_in, st));
-  PROF(c, "gemv_lmhead", gemv_bytes(lrows, H, c->V_loc),
-       gemm_dispatch(EPI_STORE, c->xs_in, lrows, H, c->lm_head, c->V_loc, c->logits, c->V_loc, nullptr, st));
+  if (!prow && fuse_norm) {
+    PROF(c, "gemv_lmhead", gemv_bytes(lrows, H, c->V_loc),
+         gemv_rms_launch(EPI_STORE, hrow, H, c->final_norm, c->cfg.eps, lrows, H, c->lm_head, c->V_loc, c->logits,
+                         c->V_loc, nullptr, st));
+  } else {
+    PROF(c, "rmsnorm", (double)lrows * H * 8.0,
+         rmsnorm_launch(hrow, prow, c->final_norm, lrows, H, c->cfg.eps, c->xn32, c->xs_in, st));
+    PROF(c, "gemv_lmhead", gemv_bytes(lrows, H, c->V_loc),
+         gemm_dispatch(EPI_STORE, c->xn32, H, c->xs_in, lrows, H, c->lm_head, c->V_loc, c->logits, c->V_loc, nullptr,
+                       st));
+  }
   if (!tp) {
     PROF(c, "argmax", (double)lrows * c->V * 4.0,
          argmax_launch(c->logits, lrows, c->V, c->V, c->argmax_d, st));
@@ -431,8 +470,8 @@ static int destroy_impl(q8_ctx* c) {
   for (auto& e : c->ev_pool) { cudaEventDestroy(e.first); cudaEventDestroy(e.second); }
   if (c->comm) ncclCommDestroy(c->comm);
   void* ptrs[] = {c->warena, c->kpool, c->vpool, c->bt_d, c->inv_freq_d, c->ids_d, c->pos_d, c->seq_d,
-                  c->qb_tok0_d, c->qb_len_d, c->argmax_d, c->hist_d, c->ctr_d, c->h, c->qkv, c->ypart,
-                  c->logits, c->part, c->xs_in, c->xs_ao, c->xs_act, c->am_val, c->am_gval, c->lg_gather,
+                  c->qb_tok0_d, c->qb_len_d, c->argmax_d, c->hist_d, c->ctr_d, c->ticket_d, c->h, c->qkv, c->ypart,
+                  c->logits, c->part, c->xs_in, c->xs_ao, c->xs_act, c->xn32, c->ao32, c->act32, c->am_val, c->am_gval, c->lg_gather,
                   c->am_idx, c->am_gidx};
   for (void* p : ptrs)
     if (p) cudaFree(p);
@@ -525,7 +564,7 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
     delete c;
     return Q8_ERR_CUDA;
   }
-  if (attention_init() != Q8_OK) {
+  if (attention_init() != Q8_OK || gemv_init() != Q8_OK) {
     delete c;
     return Q8_ERR_CUDA;
   }
@@ -611,6 +650,9 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
   if ((s = dmalloc((void**)&c->argmax_d, (size_t)rows_out * 4))) return bail(s);
   if ((s = dmalloc((void**)&c->hist_d, (size_t)c->hist_cap * rows_out * 4))) return bail(s);
   if ((s = dmalloc((void**)&c->ctr_d, 4))) return bail(s);
+  if ((s = dmalloc((void**)&c->ticket_d, (size_t)T * c->nkv * 4))) return bail(s);
+  if (cudaMemset(c->ticket_d, 0, (size_t)T * c->nkv * 4) != cudaSuccess)
+    return bail((set_error("ticket clear failed"), Q8_ERR_CUDA));
   if ((s = dmalloc((void**)&c->h, (size_t)T * H * 4))) return bail(s);
   if ((s = dmalloc((void**)&c->qkv, (size_t)T * (c->qd + 2 * c->kvd) * 4))) return bail(s);
   if (tp_size > 1 && (s = dmalloc((void**)&c->ypart, (size_t)T * H * 4))) return bail(s);
@@ -621,6 +663,9 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
   if ((s = dmalloc((void**)&c->xs_in, (size_t)T * 2 * H * 2))) return bail(s);
   if ((s = dmalloc((void**)&c->xs_ao, (size_t)T * 2 * c->qd * 2))) return bail(s);
   if ((s = dmalloc((void**)&c->xs_act, (size_t)T * 2 * c->F * 2))) return bail(s);
+  if ((s = dmalloc((void**)&c->xn32, (size_t)T * H * 4))) return bail(s);
+  if ((s = dmalloc((void**)&c->ao32, (size_t)T * c->qd * 4))) return bail(s);
+  if ((s = dmalloc((void**)&c->act32, (size_t)T * c->F * 4))) return bail(s);
   if (tp_size > 1) {
     if ((s = dmalloc((void**)&c->am_val, (size_t)rows_out * 4))) return bail(s);
     if ((s = dmalloc((void**)&c->am_idx, (size_t)rows_out * 4))) return bail(s);
@@ -960,7 +1005,8 @@ static int forward_impl(q8_ctx* c, const int32_t* ids, int s, int seq, float* lo
     const bool last = done + T == s;
     std::vector<int> lens;
     for (int i = 0; i < T; ++i) lens.push_back(pos0 + i + 1);
-    Q8_TRY(run_tokens(c, T, true, nqb, c->qb_max, nsplit, T - 1, last ? 1 : 0, kv_read_bytes(c, lens)));
+    if (T == 1) nsplit = decode_nsplit(c, 1);
+    Q8_TRY(run_tokens(c, T, T > 1, nqb, c->qb_max, nsplit, T - 1, last ? 1 : 0, kv_read_bytes(c, lens)));
     // the pinned staging is rewritten next chunk: wait for the copies
     Q8_CUDA(cudaStreamSynchronize(c->st));
     c->n_cached[seq] += T;

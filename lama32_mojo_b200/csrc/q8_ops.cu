@@ -13,6 +13,8 @@ namespace q8 {
 // k_embed_gather_q8 (src/llama_q8.mojo:96-109): y = f32(int8) * f32(f16 scale).
 __global__ void k_embed_q8(const uint8_t* __restrict__ emb, int64_t d, const int32_t* __restrict__ ids,
                            int64_t s, float* __restrict__ y) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t rb = q8_row_bytes(d);
   const int64_t total = s * d;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -27,8 +29,7 @@ __global__ void k_embed_q8(const uint8_t* __restrict__ emb, int64_t d, const int
 int embed_launch(const void* emb, int64_t d, const int32_t* ids, int64_t s, float* y, cudaStream_t st) {
   const int64_t total = s * d;
   const int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 8);
-  k_embed_q8<<<blocks, 256, 0, st>>>((const uint8_t*)emb, d, ids, s, y);
-  return launch_check("k_embed_q8");
+  return launch_pdl("k_embed_q8", k_embed_q8, dim3(blocks), dim3(256), 0, st, (const uint8_t*)emb, d, ids, s, y);
 }
 
 // ------------------------------------------------------------------ RMSNorm
@@ -39,6 +40,8 @@ __global__ void __launch_bounds__(256) k_rmsnorm(float* __restrict__ x, const fl
                                                  const uint16_t* __restrict__ w, int64_t d, float eps,
                                                  float* __restrict__ y32, __half* __restrict__ yxs) {
   __shared__ float wsum[8];
+  pdl_trigger();
+  pdl_wait();
   const int64_t r = blockIdx.x;
   float* xr = x + r * d;
   const float* rr = resid ? resid + r * d : nullptr;
@@ -73,8 +76,7 @@ __global__ void __launch_bounds__(256) k_rmsnorm(float* __restrict__ x, const fl
 int rmsnorm_launch(float* x, const float* resid, const uint16_t* w, int64_t rows, int64_t d, float eps,
                    float* y32, __half* yxs, cudaStream_t st) {
   if (rows <= 0) return Q8_OK;
-  k_rmsnorm<<<(unsigned)rows, 256, 0, st>>>(x, resid, w, d, eps, y32, yxs);
-  return launch_check("k_rmsnorm");
+  return launch_pdl("k_rmsnorm", k_rmsnorm, dim3((unsigned)rows), dim3(256), 0, st, x, resid, w, d, eps, y32, yxs);
 }
 
 // Per-head RMSNorm (Qwen3 QK-norm) — k_rmsnorm2_w (src/llama_common.mojo:228-270); warp per row.
@@ -112,6 +114,8 @@ __global__ void __launch_bounds__(256) k_rope_kv(float* __restrict__ qkv, int64_
                                                  float eps, float* __restrict__ kp, float* __restrict__ vp,
                                                  int page, const int32_t* __restrict__ bt, int max_pages) {
   constexpr int J = HD / 32;
+  pdl_trigger();
+  pdl_wait();
   const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   const int nall = nh + nkv;
@@ -170,14 +174,14 @@ int rope_kv_launch(float* qkv, int64_t ld, int64_t T, const int32_t* pos, const 
   const int blocks = ceil_div(warps, 8);
   switch (hd) {
     case 64:
-      k_rope_kv<64><<<blocks, 256, 0, st>>>(qkv, ld, T, pos, seq, nh, nkv, inv_freq, qn, kn, eps, kp, vp, page, bt, max_pages);
-      break;
+      return launch_pdl("k_rope_kv", k_rope_kv<64>, dim3(blocks), dim3(256), 0, st, qkv, ld, T, pos, seq, nh, nkv,
+                        inv_freq, qn, kn, eps, kp, vp, page, bt, max_pages);
     case 128:
-      k_rope_kv<128><<<blocks, 256, 0, st>>>(qkv, ld, T, pos, seq, nh, nkv, inv_freq, qn, kn, eps, kp, vp, page, bt, max_pages);
-      break;
+      return launch_pdl("k_rope_kv", k_rope_kv<128>, dim3(blocks), dim3(256), 0, st, qkv, ld, T, pos, seq, nh, nkv,
+                        inv_freq, qn, kn, eps, kp, vp, page, bt, max_pages);
     case 256:
-      k_rope_kv<256><<<blocks, 256, 0, st>>>(qkv, ld, T, pos, seq, nh, nkv, inv_freq, qn, kn, eps, kp, vp, page, bt, max_pages);
-      break;
+      return launch_pdl("k_rope_kv", k_rope_kv<256>, dim3(blocks), dim3(256), 0, st, qkv, ld, T, pos, seq, nh, nkv,
+                        inv_freq, qn, kn, eps, kp, vp, page, bt, max_pages);
     default:
       set_error("rope: head_dim %d unsupported (64/128/256)", hd);
       return Q8_ERR_ARG;
@@ -213,6 +217,17 @@ __device__ __forceinline__ void write_out(const AttnArgs& a, int tok, int col, f
     const int K = a.nh * a.hd;
     a.outxs[xs_index(tok, col, K, 0)] = hi;
     a.outxs[xs_index(tok, col, K, 1)] = lo;
+  }
+}
+
+__device__ __forceinline__ void write_out_tok(float* out32, int64_t ldo, __half* outxs, int K, int tok, int col,
+                                              float v) {
+  if (out32) out32[(int64_t)tok * ldo + col] = v;
+  if (outxs) {
+    __half hi, lo;
+    split_f16(v, hi, lo);
+    outxs[xs_index(tok, col, K, 0)] = hi;
+    outxs[xs_index(tok, col, K, 1)] = lo;
   }
 }
 
@@ -412,6 +427,256 @@ int attention_launch(const AttnArgs& a, cudaStream_t st) {
   }
 }
 
+// ------------------------------------------------------------------ decode attention
+// One query token per sequence (the decode step).  CTA = (token b, kv head,
+// context split), 4 warps; each warp streams a contiguous run of keys of its
+// split, lanes own head_dim/32 consecutive dims, so every K and V row is one
+// coalesced 128-bit (hd 128) or 64-bit (hd 64) load per lane.  Keys are taken 8
+// at a time (16 row loads in flight per lane) with an online softmax over the
+// GQA group's G query heads held in registers (exp2 domain: q is pre-scaled by
+// log2(e)/sqrt(hd)).  Warps merge through shared memory; splits write
+// (o, m, l) partials and the last CTA of a (token, kv head) to finish merges
+// them (atomic ticket, reset by that CTA), so no combine launch is needed.
+struct AttnDecArgs {
+  const float* q; int64_t ldq;
+  const int32_t* pos; const int32_t* seq;
+  int T, nh, nkv;
+  const float* kp; const float* vp; int page;
+  const int32_t* bt; int max_pages;
+  int nsplit;
+  float* part;      // [T*nkv][nsplit][G*HD + 2G]
+  int* ticket;      // [T*nkv], zero at rest
+  float* out32; int64_t ldo;
+  __half* outxs;
+};
+
+constexpr int ATTD_U = 4;            // keys per chunk (two chunks in flight per warp)
+constexpr int ATTD_W = 8;            // warps per CTA
+constexpr int ATTD_MAXSPLIT = 128;   // context splits per (token, kv head)
+
+template <int E>
+__device__ __forceinline__ void attd_load(const AttnDecArgs& a, const int32_t* btr, int kvh, int j0, int w_hi,
+                                          int lane, float (&kr)[ATTD_U][E], float (&vr)[ATTD_U][E]) {
+  constexpr int HD = E * 32;
+#pragma unroll
+  for (int u = 0; u < ATTD_U; ++u) {
+    const int j = min(j0 + u, w_hi - 1);
+    const int64_t off = (((int64_t)btr[j / a.page] * a.nkv + kvh) * a.page + (j % a.page)) * HD + lane * E;
+    if constexpr (E == 4) {
+      const float4 k4 = __ldg(reinterpret_cast<const float4*>(a.kp + off));
+      const float4 v4 = __ldg(reinterpret_cast<const float4*>(a.vp + off));
+      kr[u][0] = k4.x; kr[u][1] = k4.y; kr[u][2] = k4.z; kr[u][3] = k4.w;
+      vr[u][0] = v4.x; vr[u][1] = v4.y; vr[u][2] = v4.z; vr[u][3] = v4.w;
+    } else {
+      const float2 k2 = __ldg(reinterpret_cast<const float2*>(a.kp + off));
+      const float2 v2 = __ldg(reinterpret_cast<const float2*>(a.vp + off));
+      kr[u][0] = k2.x; kr[u][1] = k2.y;
+      vr[u][0] = v2.x; vr[u][1] = v2.y;
+    }
+  }
+}
+
+// online-softmax update of the G heads with one chunk of ATTD_U keys (exp2 domain)
+template <int E, int GMAX>
+__device__ __forceinline__ void attd_chunk(int G, int j0, int w_hi, const float (&q)[GMAX][E],
+                                           const float (&kr)[ATTD_U][E], const float (&vr)[ATTD_U][E],
+                                           float (&o)[GMAX][E], float (&m)[GMAX], float (&l)[GMAX]) {
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g) {
+    if (g >= G) break;
+    float sc[ATTD_U];
+#pragma unroll
+    for (int u = 0; u < ATTD_U; ++u) {
+      float d = 0.f;
+#pragma unroll
+      for (int e = 0; e < E; ++e) d = fmaf(q[g][e], kr[u][e], d);
+      sc[u] = d;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+      for (int u = 0; u < ATTD_U; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], off);
+    }
+    float mx = m[g];
+#pragma unroll
+    for (int u = 0; u < ATTD_U; ++u) {
+      if (j0 + u >= w_hi) sc[u] = -INFINITY;
+      mx = fmaxf(mx, sc[u]);
+    }
+    const float corr = (m[g] == -INFINITY) ? 0.f : exp2f(m[g] - mx);
+    float psum = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) o[g][e] *= corr;
+#pragma unroll
+    for (int u = 0; u < ATTD_U; ++u) {
+      const float pz = (sc[u] == -INFINITY) ? 0.f : exp2f(sc[u] - mx);
+      psum += pz;
+#pragma unroll
+      for (int e = 0; e < E; ++e) o[g][e] = fmaf(pz, vr[u][e], o[g][e]);
+    }
+    l[g] = l[g] * corr + psum;
+    m[g] = mx;
+  }
+}
+
+template <int HD, int GMAX>
+__global__ void __launch_bounds__(ATTD_W * 32, 2) k_attn_decode(AttnDecArgs a) {
+  constexpr int E = HD / 32;
+  pdl_trigger();
+  pdl_wait();
+  const int item = blockIdx.x, sp = blockIdx.y;
+  const int b = item / a.nkv, kvh = item % a.nkv;
+  const int G = a.nh / a.nkv;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kv_end = a.pos[b] + 1;
+  const int per = (kv_end + a.nsplit - 1) / a.nsplit;
+  const int k_lo = min(kv_end, sp * per), k_hi = min(kv_end, k_lo + per);
+  const int wper = (k_hi - k_lo + ATTD_W - 1) / ATTD_W;
+  const int w_lo = min(k_hi, k_lo + warp * wper), w_hi = min(k_hi, w_lo + wper);
+  const float qscale = 1.4426950408889634f / sqrtf((float)HD);  // log2(e)/sqrt(hd): exp2 domain
+
+  float q[GMAX][E], o[GMAX][E], m[GMAX], l[GMAX];
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      o[g][e] = 0.f;
+      q[g][e] = (g < G) ? a.q[(int64_t)b * a.ldq + (int64_t)(kvh * G + g) * HD + lane * E + e] * qscale : 0.f;
+    }
+  }
+  const int32_t* btr = a.bt + (int64_t)a.seq[b] * a.max_pages;
+  if (w_lo < w_hi) {
+    float k0[ATTD_U][E], v0[ATTD_U][E], k1[ATTD_U][E], v1[ATTD_U][E];
+    attd_load<E>(a, btr, kvh, w_lo, w_hi, lane, k0, v0);
+    for (int j0 = w_lo; j0 < w_hi; j0 += 2 * ATTD_U) {
+      const int j1 = j0 + ATTD_U;
+      if (j1 < w_hi) attd_load<E>(a, btr, kvh, j1, w_hi, lane, k1, v1);
+      attd_chunk<E, GMAX>(G, j0, w_hi, q, k0, v0, o, m, l);
+      if (j1 < w_hi) {
+        if (j1 + ATTD_U < w_hi) attd_load<E>(a, btr, kvh, j1 + ATTD_U, w_hi, lane, k0, v0);
+        attd_chunk<E, GMAX>(G, j1, w_hi, q, k1, v1, o, m, l);
+      }
+    }
+  }
+
+  // merge the warps: (m, l, o) per head
+  __shared__ float sm_m[ATTD_W][GMAX], sm_l[ATTD_W][GMAX];
+  __shared__ float sm_o[ATTD_W][GMAX][HD];
+  __shared__ int s_last;
+  if (lane == 0) {
+#pragma unroll
+    for (int g = 0; g < GMAX; ++g) {
+      sm_m[warp][g] = m[g];
+      sm_l[warp][g] = l[g];
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g) {
+    if (g >= G) break;
+#pragma unroll
+    for (int e = 0; e < E; ++e) sm_o[warp][g][lane * E + e] = o[g][e];
+  }
+  __syncthreads();
+  const int W = G * HD + 2 * G;
+  float* mypart = a.part + ((int64_t)item * a.nsplit + sp) * W;
+  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+    const int g = i / HD, d = i % HD;
+    float M = -INFINITY;
+    for (int w = 0; w < ATTD_W; ++w) M = fmaxf(M, sm_m[w][g]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+      for (int w = 0; w < ATTD_W; ++w) {
+        if (sm_m[w][g] == -INFINITY) continue;
+        const float f = exp2f(sm_m[w][g] - M);
+        L = fmaf(sm_l[w][g], f, L);
+        O = fmaf(sm_o[w][g][d], f, O);
+      }
+    }
+    if (a.nsplit == 1) {
+      write_out_tok(a.out32, a.ldo, a.outxs, a.nh * HD, b, (kvh * G + g) * HD + d, L > 0.f ? O / L : 0.f);
+    } else {
+      mypart[i] = O;
+      if (d == 0) {
+        mypart[G * HD + g] = M;
+        mypart[G * HD + G + g] = L;
+      }
+    }
+  }
+  if (a.nsplit == 1) return;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atomicAdd(&a.ticket[item], 1) == a.nsplit - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // merge the splits: per-split weights exp2(m_s - M) once in shared memory,
+  // then each output sums the partials in rounds of 16 independent loads
+  const float* base = a.part + (int64_t)item * a.nsplit * W;
+  __shared__ float s_w[GMAX][ATTD_MAXSPLIT];
+  __shared__ float s_l[GMAX][ATTD_MAXSPLIT];
+  __shared__ float s_L[GMAX];
+  for (int idx = threadIdx.x; idx < G * a.nsplit; idx += blockDim.x) {
+    const int g = idx / a.nsplit, s2 = idx % a.nsplit;
+    s_w[g][s2] = __ldcg(base + (int64_t)s2 * W + G * HD + g);
+    s_l[g][s2] = __ldcg(base + (int64_t)s2 * W + G * HD + G + g);
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int g = threadIdx.x;
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < a.nsplit; ++s2) M = fmaxf(M, s_w[g][s2]);
+    float L = 0.f;
+    for (int s2 = 0; s2 < a.nsplit; ++s2) {
+      const float f = (M == -INFINITY || s_w[g][s2] == -INFINITY) ? 0.f : exp2f(s_w[g][s2] - M);
+      s_w[g][s2] = f;
+      L = fmaf(s_l[g][s2], f, L);
+    }
+    s_L[g] = L;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+    const int g = i / HD, d = i % HD;
+    float O = 0.f;
+    for (int s0 = 0; s0 < a.nsplit; s0 += 16) {
+      float v[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) v[u] = (s0 + u < a.nsplit) ? __ldcg(base + (int64_t)(s0 + u) * W + i) : 0.f;
+#pragma unroll
+      for (int u = 0; u < 16; ++u)
+        if (s0 + u < a.nsplit) O = fmaf(v[u], s_w[g][s0 + u], O);
+    }
+    const float L = s_L[g];
+    write_out_tok(a.out32, a.ldo, a.outxs, a.nh * HD, b, (kvh * G + g) * HD + d, L > 0.f ? O / L : 0.f);
+  }
+  if (threadIdx.x == 0) a.ticket[item] = 0;  // ready for the next launch
+}
+
+size_t attention_decode_part_floats(int T, int nkv, int nsplit, int group, int hd) {
+  return (size_t)T * nkv * nsplit * (size_t)(group * hd + 2 * group);
+}
+
+int attention_decode_launch(const float* q, int64_t ldq, int T, const int32_t* pos, const int32_t* seq, int nh,
+                            int nkv, int hd, const float* kp, const float* vp, int page, const int32_t* bt,
+                            int max_pages, int nsplit, float* part, int* ticket, float* out32, int64_t ldo,
+                            __half* outxs, cudaStream_t st) {
+  Q8_CHECK_ARG(nkv > 0 && nh % nkv == 0 && nh / nkv <= 8, "attention decode: GQA group must be <= 8");
+  Q8_CHECK_ARG(nsplit >= 1 && nsplit <= ATTD_MAXSPLIT && (nsplit == 1 || (part && ticket)),
+               "attention decode: bad split count %d", nsplit);
+  if (T <= 0) return Q8_OK;
+  AttnDecArgs a{q, ldq, pos, seq, T, nh, nkv, kp, vp, page, bt, max_pages, nsplit, part, ticket, out32, ldo, outxs};
+  dim3 grid(T * nkv, nsplit);
+  const bool g4 = nh / nkv <= 4;
+  const dim3 blk(ATTD_W * 32);
+  if (hd == 128 && g4) return launch_pdl("k_attn_decode", k_attn_decode<128, 4>, grid, blk, 0, st, a);
+  if (hd == 128) return launch_pdl("k_attn_decode", k_attn_decode<128, 8>, grid, blk, 0, st, a);
+  if (hd == 64 && g4) return launch_pdl("k_attn_decode", k_attn_decode<64, 4>, grid, blk, 0, st, a);
+  if (hd == 64) return launch_pdl("k_attn_decode", k_attn_decode<64, 8>, grid, blk, 0, st, a);
+  set_error("attention decode: head_dim %d unsupported", hd);
+  return Q8_ERR_ARG;
+}
+
 // ------------------------------------------------------------------ argmax
 // k_argmax (src/llama_common.mojo:493-519): one CTA per row; lowest index wins
 // ties (numpy.argmax), where the reference's 32-lane tree keeps the lower lane.
@@ -419,6 +684,8 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ x, in
                                                  int32_t* __restrict__ out) {
   __shared__ float sv[32];
   __shared__ int si[32];
+  pdl_trigger();
+  pdl_wait();
   const float* row = x + (int64_t)blockIdx.x * ld;
   float bv = -INFINITY;
   int bi = 0x7fffffff;
@@ -463,8 +730,7 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ x, in
 
 int argmax_launch(const float* logits, int64_t rows, int64_t n, int64_t ld, int32_t* out, cudaStream_t st) {
   if (rows <= 0) return Q8_OK;
-  k_argmax<<<(unsigned)rows, 1024, 0, st>>>(logits, n, ld, out);
-  return launch_check("k_argmax");
+  return launch_pdl("k_argmax", k_argmax, dim3((unsigned)rows), dim3(1024), 0, st, logits, n, ld, out);
 }
 
 }  // namespace q8
@@ -508,24 +774,29 @@ extern "C" int q8op_attention(const float* q, int64_t ldq, int64_t T, const int3
                               int page, const int32_t* block_table, int max_pages, float* out, int64_t ldo,
                               void* stream) {
   Q8_CHECK_ARG(q && pos && seq && k_pages && v_pages && block_table && out, "q8op_attention: null");
-  Q8_CHECK_ARG(T >= 0 && T < (1 << 30) && n_kv > 0 && n_heads % n_kv == 0 && page > 0,
+  Q8_CHECK_ARG(T >= 0 && T < (1 << 24) && n_kv > 0 && n_heads % n_kv == 0 && page > 0,
                "q8op_attention: bad shape");
   if (T == 0) return Q8_OK;
-  Q8_TRY(attention_init());
-  AttnArgs a{};
-  a.q = q; a.ldq = ldq; a.T = (int)T; a.pos = pos; a.seq = seq;
-  a.nh = n_heads; a.nkv = n_kv; a.hd = hd; a.kp = k_pages; a.vp = v_pages; a.page = page;
-  a.bt = block_table; a.max_pages = max_pages;
-  a.qb_tok0 = nullptr; a.qb_len = nullptr; a.nqb = (int)T; a.qb_max = 1;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int G = n_heads / n_kv;
   const int items = (int)T * n_kv;
-  a.nsplit = std::max(1, std::min(32, ceil_div(2 * num_sms(), items)));
-  a.out32 = out; a.ldo = ldo; a.outxs = nullptr;
-  if (a.nsplit > 1) {
-    void* part = nullptr;
-    Q8_TRY(op_scratch(attention_part_floats(a.nqb, n_kv, a.nsplit, 1, n_heads / n_kv, hd) * 4, &part));
-    a.part = (float*)part;
+  // every token is an independent query (one per item); split the context so
+  // that the grid covers the GPU (at most max_pages*page/64 keys per split)
+  int nsplit = std::max(1, std::min(ceil_div(2 * num_sms(), items), ceil_div((int64_t)max_pages * page, 64)));
+  nsplit = std::min(nsplit, ATTD_MAXSPLIT);
+  float* part = nullptr;
+  int* ticket = nullptr;
+  if (nsplit > 1) {
+    const size_t pf = attention_decode_part_floats((int)T, n_kv, nsplit, G, hd);
+    void* scr = nullptr;
+    const size_t pbytes = (pf * 4 + 255) & ~(size_t)255;
+    Q8_TRY(op_scratch(pbytes + (size_t)items * 4, &scr));
+    part = (float*)scr;
+    ticket = (int*)((char*)scr + pbytes);
+    Q8_CUDA(cudaMemsetAsync(ticket, 0, (size_t)items * 4, st));
   }
-  return attention_launch(a, (cudaStream_t)stream);
+  return attention_decode_launch(q, ldq, (int)T, pos, seq, n_heads, n_kv, hd, k_pages, v_pages, page, block_table,
+                                 max_pages, nsplit, part, ticket, out, ldo, nullptr, st);
 }
 
 extern "C" int q8op_argmax(const float* logits, int64_t rows, int64_t n, int64_t ld, int32_t* out, void* stream) {

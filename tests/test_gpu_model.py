@@ -217,3 +217,24 @@ def test_load_safetensors_packed_and_bf16(cuda, tmp_path, golden_dir, packed):
     (tmp_path / "model.safetensors").write_bytes(raw[:-64])
     with pytest.raises(Q8Error):
         load_q8(str(tmp_path), maxlen=32)
+
+
+@pytest.mark.parametrize("cfgname", ["tiny-llama", "tiny-qwen3"])
+def test_large_prefill_chunk_and_wide_batch(cuda, cfgname):
+    """A 100-token prefill in one chunk (standalone RMSNorm + multi-tile GEMM
+    path) and a 12-sequence decode batch (two token tiles) against the oracle."""
+    ocfg = O.PRESETS[cfgname]
+    ck = O.make_q8_checkpoint(ocfg)
+    ids = O.random_ids(ocfg, 100, seed=8)
+    m = build(cfgname, maxlen=128, max_tokens=128, max_seqs=12)
+    close(m.forward(ids, seq=0), O.OracleModel(ocfg, ck).forward(ids))
+    prompts = [O.random_ids(ocfg, 2 + s, seed=30 + s) for s in range(12)]
+    for s in range(1, 12):
+        m.forward(prompts[s], seq=s)
+    toks = [int(t) for t in np.random.default_rng(0).integers(0, ocfg.vocab, 12)]
+    am, lg = m.decode(toks, list(range(12)), logits=True)
+    for s in range(12):
+        o = O.OracleModel(ocfg, ck)
+        o.forward(ids if s == 0 else prompts[s])
+        close(lg[s], o.forward([toks[s]]))
+        assert int(am[s]) == int(np.argmax(lg[s]))
