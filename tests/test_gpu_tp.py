@@ -1,0 +1,95 @@
+"""Tensor parallelism on 2 GPUs: each rank loads the same checkpoint, the
+loader slices its shard (q8_shard_plan), the row-parallel partials are summed
+with NCCL inside the library.  Rank 0's logits, per-layer hidden states and
+greedy tokens must match the single-GPU oracle.  Skipped with fewer than 2 GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import q8_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank(rank, world, port, cfgname, ids, steps, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    from lama32_mojo_b200 import PRESETS
+    from lama32_mojo_b200.model import Q8Model, nccl_unique_id
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    try:
+        uid = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        m = Q8Model(PRESETS[cfgname], device=rank, maxlen=64, max_seqs=2, tp_rank=rank, tp_size=world,
+                    nccl_id=uid[0])
+        for name, w in O.make_bf16_weights(O.PRESETS[cfgname], 0):
+            m.load_tensor(name, w, packed=False)
+        out = {"hidden1": m.forward_hidden(ids, 1)}
+        out["logits"] = m.forward(ids)
+        toks = [int(np.argmax(out["logits"]))]
+        for _ in range(steps):
+            toks.append(m.forward_argmax([toks[-1]]))
+        out["tokens"] = toks
+        m.forward(ids[:3], seq=1)
+        out["gen"] = m.generate([toks[0]], [1], 3)[:, 0].tolist()
+        m.close()
+        if rank == 0:
+            q.put(out)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("cfgname", ["tiny-llama", "tiny-qwen3", "tiny-llama-untied"])
+def test_tp2_matches_oracle(cuda, cfgname):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ocfg = O.PRESETS[cfgname]
+    ids = O.random_ids(ocfg, 9, seed=41)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, cfgname, ids, 4, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        out = q.get(timeout=300)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    assert all(p.exitcode == 0 for p in procs)
+    ck = O.make_q8_checkpoint(ocfg)
+    orc = O.OracleModel(ocfg, ck)
+    ref = orc.forward(ids)
+    assert O.rel_l2(out["hidden1"], orc.trace["after_layer1"]) < 1e-5
+    assert O.rel_l2(out["logits"], ref) < 1e-5 and np.abs(out["logits"] - ref).max() < 2e-2
+    toks = [int(np.argmax(ref))]
+    for _ in range(4):
+        toks.append(orc.forward_argmax([toks[-1]]))
+    assert out["tokens"] == toks
+    o2 = O.OracleModel(ocfg, ck)
+    o2.forward(ids[:3])
+    want = []
+    t = toks[0]
+    for _ in range(3):
+        t = o2.forward_argmax([t])
+        want.append(t)
+    assert out["gen"] == want
