@@ -74,6 +74,12 @@ const char* q8_last_error(const q8_ctx* ctx);
 const char* q8_status_string(int status);
 /* Library build string (arch, version). */
 const char* q8_version(void);
+/* Synchronizes the current device, then reports and clears a timeout that a
+   bounded barrier wait inside a tensor-core GEMM recorded (Q8_ERR_TIMEOUT),
+   else Q8_OK.  The model entry points poll this themselves after a prefill;
+   op-level callers poll it when they synchronize.  No counterpart in the
+   reference (its kernels have no device-side waits). */
+int q8_device_status(void);
 
 /* =================================================================== op level */
 

@@ -74,6 +74,9 @@ __device__ __forceinline__ void split_f16(float v, __half& hi, __half& lo) {
   lo = __float2half_rn(v - __half2float(hi));
 }
 
+// SwiGLU activation silu(g) * u — k_swiglu_mul (src/llama_common.mojo:476).
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+
 __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
   return __uint_as_float(((uint32_t)b) << 16);
 }
@@ -139,6 +142,8 @@ static __device__ int g_q8_device_error;
 // a lost completion never hangs the GPU.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
+  // once any wait has given up, later ones return at once so the grid drains
+  if (*reinterpret_cast<volatile int*>(&g_q8_device_error)) return false;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
     if (clock64() - t0 > (1ll << 31)) {

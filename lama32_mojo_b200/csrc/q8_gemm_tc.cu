@@ -1,0 +1,399 @@
+// Prefill Q8 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// Replaces k_mm_q8 / mm_q8_op for large token counts (src/llama_q8.mojo:54-141)
+// and, with the SwiGLU epilogue, the gate/up GEMM + k_swiglu_mul pair
+// (src/llama_common.mojo:476):
+//   y[m, n] (+)= sum_k x16[m, k] * f16(q[n, k] * s[n, k/64])
+//
+// Tile: 128 weight rows (MMA M) x 128 tokens (MMA N), K in steps of 64 (one
+// quantization group).  Warp roles (192 threads):
+//   warp 0     TMA producer: two int8 code boxes [64 rows x 64 B] (no swizzle)
+//              and the f16 activation box [128 tokens x 128 B] (128 B swizzle)
+//              into a 4-stage ring; completion counted in bytes on full[s].
+//   warps 2-5  dequantize codes x f16 group scale -> f16 (one rounding of the
+//              exact product) into the K-major 128 B-swizzled layout the
+//              tensor core reads; fence to the async proxy; arrive conv[s].
+//   warp 1     allocates 128 TMEM columns; one lane issues 4 x
+//              tcgen05.mma.kind::f16 (K = 16 each, f32 accumulate in TMEM) per
+//              stage and commits the stage back to empty[s].
+// Epilogue (warps 2-5, each owning the 32 TMEM lanes = weight rows of its
+// quadrant): tcgen05.ld.32x32b, then store / accumulate y[token][row]
+// (consecutive lanes -> consecutive rows: coalesced).  SwiGLU tiles hold 64
+// gate rows in lanes 0-63 and the matching up rows in lanes 64-127; the up
+// quadrants hand their values to the gate quadrants through shared memory.
+//
+// Every barrier wait is bounded (mbar_wait): a lost completion records
+// Q8_ERR_TIMEOUT in the device error word instead of hanging, and the CTA
+// still releases its TMEM.  No load uses cluster multicast.
+#include "q8_kernels.h"
+
+#include <cuda.h>
+
+#include <mutex>
+
+namespace q8 {
+
+constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 64, TC_S = 4;
+constexpr int TC_CODES = TC_BM * TC_BK;          // 8 KB int8
+constexpr int TC_A = TC_BM * TC_BK * 2;          // 16 KB f16, SW128
+constexpr int TC_B = TC_BN * TC_BK * 2;          // 16 KB f16, SW128
+constexpr int TC_STAGE = TC_A + TC_B + TC_CODES; // 40 KB: A and B stay 1024 B aligned
+constexpr int TC_SMEM = TC_S * TC_STAGE + 1024;  // + alignment slack
+static_assert(TC_STAGE % 1024 == 0, "stage must keep 1024 B alignment for SW128");
+
+struct TcParams {
+  const uint8_t* W;  // packed rows (group scales read from here)
+  int64_t rb;        // packed row bytes
+  int K, N, M;       // N: output rows (SwiGLU: pairs F; W holds 2F rows)
+  float* y;          // f32 output [M][ldy] (nullable for SwiGLU)
+  int64_t ldy;
+  __half* y16;       // SwiGLU only: f16 copy of the output [M][ld16]
+  int64_t ld16;
+};
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor, K-major with 128 B swizzle: start >> 4,
+// LBO 16 B (ignored for swizzled K-major), SBO 1024 B (8 rows x 128 B),
+// descriptor version 1, layout type 2 (SWIZZLE_128B).
+__device__ __forceinline__ uint64_t sw128_desc(const void* smem_ptr) {
+  const uint64_t addr = smem_u32(smem_ptr);
+  return ((addr >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+__device__ __forceinline__ void tc_mma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 16 int8 codes (one uint4) times the f16 group scale -> 16 f16 values.
+// Bytes are biased to u8, placed as the low mantissa byte of 1024.0h and the
+// 1152.0h bias removed: exact integers q, then one rounding of q * s.
+__device__ __forceinline__ void dequant16(uint4 c, __half2 s2, uint32_t (&h)[8]) {
+  const uint32_t w[4] = {c.x ^ 0x80808080u, c.y ^ 0x80808080u, c.z ^ 0x80808080u, c.w ^ 0x80808080u};
+  const uint32_t k1152 = 0x64806480u;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t lo = __byte_perm(w[j], 0x64646464u, 0x5140), hi = __byte_perm(w[j], 0x64646464u, 0x5342);
+    __half2 a = __hsub2(*reinterpret_cast<__half2*>(&lo), *reinterpret_cast<const __half2*>(&k1152));
+    __half2 b = __hsub2(*reinterpret_cast<__half2*>(&hi), *reinterpret_cast<const __half2*>(&k1152));
+    a = __hmul2(a, s2);
+    b = __hmul2(b, s2);
+    h[2 * j] = *reinterpret_cast<uint32_t*>(&a);
+    h[2 * j + 1] = *reinterpret_cast<uint32_t*>(&b);
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(192, 1) k_gemm_q8_tc(const __grid_constant__ CUtensorMap tm_codes,
+                                                       const __grid_constant__ CUtensorMap tm_x, TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  // 1024 B alignment of the shared-window address (the swizzle atom)
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  __shared__ __align__(8) uint64_t full[TC_S], conv[TC_S], empty[TC_S], accf;
+  __shared__ uint32_t tmem_base;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // token tiles vary fastest: CTAs resident together share one weight tile
+  const int m0 = blockIdx.x * TC_BN;
+  const int r0 = blockIdx.y * (EPI == EPI_SWIGLU ? TC_BM / 2 : TC_BM);  // first output row (pair)
+  // weight rows of the two 64-row code boxes
+  const int rowA = r0, rowB = (EPI == EPI_SWIGLU) ? p.N + r0 : r0 + 64;
+  const int nk = p.K / TC_BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TC_S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], 4);  // one arrive per converter warp
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&accf, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                 "r"(TC_BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_base;
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      for (int kt = 0; kt < nk; ++kt) {
+        const int s = kt % TC_S;
+        const uint32_t ph = (kt / TC_S) & 1;
+        mbar_wait(&empty[s], ph ^ 1);
+        uint8_t* st = smem + s * TC_STAGE;
+        mbar_arrive_expect_tx(&full[s], TC_CODES + TC_B);
+        tma_load_2d(st + TC_A + TC_B, &tm_codes, kt * TC_BK, rowA, &full[s]);
+        tma_load_2d(st + TC_A + TC_B + TC_CODES / 2, &tm_codes, kt * TC_BK, rowB, &full[s]);
+        tma_load_2d(st + TC_A, &tm_x, kt * TC_BK, m0, &full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    // instruction descriptor: f32 accumulate, A = B = f16, both K-major,
+    // N = 128 (bits 17-22: N >> 3), M = 128 (bits 24-28: M >> 4)
+    const uint32_t idesc = (1u << 4) | ((uint32_t)(TC_BN >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+    if (lane == 0) {
+      for (int kt = 0; kt < nk; ++kt) {
+        const int s = kt % TC_S;
+        const uint32_t ph = (kt / TC_S) & 1;
+        mbar_wait(&full[s], ph);
+        mbar_wait(&conv[s], ph);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        uint8_t* st = smem + s * TC_STAGE;
+        const uint64_t da = sw128_desc(st), db = sw128_desc(st + TC_A);
+#pragma unroll
+        for (int k = 0; k < TC_BK / 16; ++k)  // K = 16 -> 32 B further inside the swizzle atom
+          tc_mma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (kt | k) != 0);
+        tc_commit(&empty[s]);
+      }
+      tc_commit(&accf);
+    }
+  } else {
+    // ---------------- converters (128 threads), then the epilogue
+    const int ct = threadIdx.x - 64;
+    // item it of thread ct: A row (it*128 + ct) >> 2, 16-code chunk (it*128 + ct) & 3
+    const __half* srow[4];
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int row = (it * 128 + ct) >> 2;
+      int n;
+      bool ok;
+      if constexpr (EPI == EPI_SWIGLU) {
+        ok = r0 + (row & 63) < p.N;
+        n = (row < 64 ? rowA : rowB) + (row & 63);
+      } else {
+        n = r0 + row;
+        ok = n < p.N;
+      }
+      srow[it] = ok ? reinterpret_cast<const __half*>(p.W + (int64_t)n * p.rb) : nullptr;
+    }
+    for (int kt = 0; kt < nk; ++kt) {
+      const int s = kt % TC_S;
+      const uint32_t ph = (kt / TC_S) & 1;
+      __half sc[4];
+#pragma unroll
+      for (int it = 0; it < 4; ++it) sc[it] = srow[it] ? srow[it][kt] : __float2half(0.f);
+      mbar_wait(&full[s], ph);
+      uint8_t* st = smem + s * TC_STAGE;
+      const uint8_t* codes = st + TC_A + TC_B;
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int idx = it * 128 + ct;
+        const int row = idx >> 2, chunk = idx & 3;
+        uint32_t h[8];
+        dequant16(*reinterpret_cast<const uint4*>(codes + row * TC_BK + chunk * 16), __halves2half2(sc[it], sc[it]),
+                  h);
+        // 16 f16 = logical 16-byte chunks 2*chunk and 2*chunk+1 of the 128 B row
+        uint8_t* arow = st + row * 128;
+        *reinterpret_cast<uint4*>(arow + (((2 * chunk) ^ (row & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4*>(arow + (((2 * chunk + 1) ^ (row & 7)) << 4)) = make_uint4(h[4], h[5], h[6], h[7]);
+      }
+      fence_async_shared();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&conv[s]);
+    }
+    // ---------------- epilogue: this warp's TMEM lanes are A rows 32q..32q+31
+    mbar_wait(&accf, 0);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const int q = warp & 3;
+    const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16);
+    if constexpr (EPI == EPI_SWIGLU) {
+      // every MMA has completed: stage memory is free for the hand-off
+      float* xch = reinterpret_cast<float*>(smem);  // [64 rows][33]
+      const int pr = r0 + 32 * (q & 1) + lane;
+#pragma unroll 1
+      for (int c0 = 0; c0 < TC_BN; c0 += 32) {
+        float v[32];
+        tmem_ld32(tq + (uint32_t)c0, v);
+        if (q >= 2) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) xch[(32 * (q - 2) + lane) * 33 + j] = v[j];
+        }
+        epi_bar();
+        if (q < 2 && pr < p.N) {
+#pragma unroll 4
+          for (int j = 0; j < 32; ++j) {
+            const int m = m0 + c0 + j;
+            if (m < p.M) {
+              const float a = silu_mul(v[j], xch[(32 * q + lane) * 33 + j]);
+              if (p.y) p.y[(int64_t)m * p.ldy + pr] = a;
+              if (p.y16) p.y16[(int64_t)m * p.ld16 + pr] = __float2half_rn(a);
+            }
+          }
+        }
+        epi_bar();
+      }
+    } else {
+      const int n = r0 + 32 * q + lane;
+#pragma unroll 1
+      for (int c0 = 0; c0 < TC_BN; c0 += 32) {
+        float v[32];
+        tmem_ld32(tq + (uint32_t)c0, v);
+        if (n < p.N) {
+#pragma unroll 4
+          for (int j = 0; j < 32; ++j) {
+            const int m = m0 + c0 + j;
+            if (m < p.M) {
+              float* dst = p.y + (int64_t)m * p.ldy + n;
+              if constexpr (EPI == EPI_ADD) *dst += v[j];
+              else *dst = v[j];
+            }
+          }
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_BN) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------- host side
+typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                      const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                      CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled_t encode_fn() {
+  static PFN_encodeTiled_t fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_encodeTiled_t)f;
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+static int tc_init() {
+  static bool done[64] = {false};
+  static std::mutex mu;
+  int dev = 0;
+  Q8_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(mu);
+  if (done[dev & 63]) return Q8_OK;
+  Q8_CUDA(cudaFuncSetAttribute(k_gemm_q8_tc<EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
+  Q8_CUDA(cudaFuncSetAttribute(k_gemm_q8_tc<EPI_ADD>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
+  Q8_CUDA(cudaFuncSetAttribute(k_gemm_q8_tc<EPI_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
+  done[dev & 63] = true;
+  return Q8_OK;
+}
+
+bool gemm_tc_supported(int K, const void* W, const __half* x16, int64_t ld16) {
+  return K > 0 && K % 512 == 0 && ((uintptr_t)W & 15) == 0 && x16 && ((uintptr_t)x16 & 15) == 0 && ld16 >= K &&
+         (ld16 * 2) % 16 == 0 && encode_fn() != nullptr;
+}
+
+int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int M, int K, const void* W, int N, float* y,
+                   int64_t ldy, __half* y16, int64_t ldy16, cudaStream_t st) {
+  if (M <= 0 || N <= 0) return Q8_OK;
+  Q8_CHECK_ARG(gemm_tc_supported(K, W, x16, ld16),
+               "gemm_tc: unsupported operands (K=%d must be a multiple of 512; 16-byte aligned W and x)", K);
+  Q8_CHECK_ARG(epi == EPI_SWIGLU ? (y || y16) : y != nullptr, "gemm_tc: no output");
+  Q8_CHECK_ARG(epi != EPI_SWIGLU || !y16 || (((uintptr_t)y16 & 1) == 0 && ldy16 >= N), "gemm_tc: bad y16");
+  Q8_TRY(tc_init());
+  PFN_encodeTiled_t enc = encode_fn();
+  const int64_t rb = q8_row_bytes(K);
+  const int wrows = epi == EPI_SWIGLU ? 2 * N : N;
+  CUtensorMap tmc, tmx;
+  {
+    // codes of every row: K bytes after the K/32 bytes of f16 group scales
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)wrows};
+    cuuint64_t strides[1] = {(cuuint64_t)rb};
+    cuuint32_t box[2] = {TC_BK, TC_BM / 2};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(&tmc, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)((const uint8_t*)W + K / 32), dims, strides, box,
+                     es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      set_error("gemm_tc: code tensor map encode failed (%d)", (int)r);
+      return Q8_ERR_CUDA;
+    }
+  }
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld16 * 2)};
+    cuuint32_t box[2] = {TC_BK, TC_BN};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(&tmx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)x16, dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      set_error("gemm_tc: activation tensor map encode failed (%d)", (int)r);
+      return Q8_ERR_CUDA;
+    }
+  }
+  TcParams p{(const uint8_t*)W, rb, K, N, M, y, ldy, y16, ldy16};
+  dim3 grid(ceil_div(M, TC_BN), epi == EPI_SWIGLU ? ceil_div(N, TC_BM / 2) : ceil_div(N, TC_BM));
+  if (epi == EPI_STORE) k_gemm_q8_tc<EPI_STORE><<<grid, 192, TC_SMEM, st>>>(tmc, tmx, p);
+  else if (epi == EPI_ADD) k_gemm_q8_tc<EPI_ADD><<<grid, 192, TC_SMEM, st>>>(tmc, tmx, p);
+  else k_gemm_q8_tc<EPI_SWIGLU><<<grid, 192, TC_SMEM, st>>>(tmc, tmx, p);
+  return launch_check("k_gemm_q8_tc");
+}
+
+int gemm_tc_poll_error() {
+  int v = 0;
+  Q8_CUDA(cudaMemcpyFromSymbol(&v, g_q8_device_error, sizeof(int)));
+  if (v == 0) return Q8_OK;
+  const int z = 0;
+  Q8_CUDA(cudaMemcpyToSymbol(g_q8_device_error, &z, sizeof(int)));
+  set_error("k_gemm_q8_tc: a pipeline barrier wait timed out (device status %d)", v);
+  return v;
+}
+
+}  // namespace q8
+
+extern "C" int q8_device_status(void) {
+  Q8_CUDA(cudaDeviceSynchronize());
+  return q8::gemm_tc_poll_error();
+}

@@ -94,8 +94,6 @@ __device__ __forceinline__ void load_codes16(const uint8_t* p, uint32_t c[4]) {
   }
 }
 
-__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
-
 // Row addresses of lane (g, t) for a row tile: rows g and g+8 (SWIGLU: gate
 // pair p and its up row F + p).
 template <int EPI>
@@ -607,6 +605,28 @@ int to_f32_launch(const void* x, int dtype, int64_t ldx, int M, int K, float* y,
   return launch_check("k_to_f32");
 }
 
+__global__ void k_to_f16(const void* __restrict__ x, int dtype, int64_t ldx, int M, int K, __half* __restrict__ y) {
+  const int64_t total = (int64_t)M * K;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / K, k = i % K;
+    if (dtype == Q8_F16) {
+      y[i] = reinterpret_cast<const __half*>(x)[m * ldx + k];
+      continue;
+    }
+    const float v = dtype == Q8_F32 ? reinterpret_cast<const float*>(x)[m * ldx + k]
+                                    : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[m * ldx + k]);
+    y[i] = __float2half_rn(v);
+  }
+}
+
+int to_f16_launch(const void* x, int dtype, int64_t ldx, int M, int K, __half* y, cudaStream_t st) {
+  const int64_t total = (int64_t)M * K;
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 16);
+  k_to_f16<<<blocks, 256, 0, st>>>(x, dtype, ldx, M, K, y);
+  return launch_check("k_to_f16");
+}
+
 int to_xs_launch(const void* x, int dtype, int64_t ldx, int M, int K, __half* xs, cudaStream_t st) {
   const int64_t total = (int64_t)M * K;
   const int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 16);
@@ -863,6 +883,12 @@ static int op_gemm_common(int epi, const void* x, int x_dtype, int64_t ldx, int6
   Q8_CHECK_ARG(M < (1 << 30) && K < (1 << 30) && N < (1 << 30), "q8op_gemm: dims too large");
   cudaStream_t st = (cudaStream_t)stream;
   void* xs = nullptr;
+  if (M >= kTcMinTokens && K % 512 == 0 && ((uintptr_t)w & 15) == 0) {
+    // prefill-sized batch: f16 rows -> tensor-core GEMM
+    Q8_TRY(op_scratch((size_t)M * K * 2, &xs));
+    Q8_TRY(to_f16_launch(x, x_dtype, ldx, (int)M, (int)K, (__half*)xs, st));
+    return gemm_tc_launch(epi, (const __half*)xs, K, (int)M, (int)K, w, (int)N, y, ldy, nullptr, 0, st);
+  }
   Q8_TRY(op_scratch((size_t)M * K * 8, &xs));
   Q8_TRY(to_xs_launch(x, x_dtype, ldx, (int)M, (int)K, (__half*)xs, st));
   // f32 rows for the int8-digit kernel: the caller's x when it is f32, else a

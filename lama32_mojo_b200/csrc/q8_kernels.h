@@ -16,16 +16,31 @@ int gemv_rms_launch(int epi, const float* h, int64_t ldh, const uint16_t* nw, fl
 // the other covers the shape.
 int gemv_launch(int epi, const float* x32, int64_t ldx32, const __half* xs, int M, int K, const void* W, int N,
                 float* y, int64_t ldy, __half* ys, cudaStream_t st);
-// Chooses the decode GEMV kernels or (later) the tensor-core tile GEMM by M.
+// Decode-shaped GEMMs (the GEMV kernels above); prefill-sized batches go to
+// gemm_tc_launch.
 int gemm_dispatch(int epi, const float* x32, int64_t ldx32, const __half* xs, int M, int K, const void* W, int N,
                   float* y, int64_t ldy, __half* ys, cudaStream_t st);
 int op_scratch(size_t bytes, void** out);
 
+// Tensor-core GEMM (tcgen05/TMEM) for prefill batches: x16 plain f16 rows
+// [M][ld16]; K a multiple of 512.  STORE/ADD write y (f32); SWIGLU (N = F
+// pairs, W = 2F rows gate|up) writes y and/or y16 (f16 rows [M][ldy16]).
+bool gemm_tc_supported(int K, const void* W, const __half* x16, int64_t ld16);
+int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int M, int K, const void* W, int N, float* y,
+                   int64_t ldy, __half* y16, int64_t ldy16, cudaStream_t st);
+// After a synchronize: Q8_OK, or the timeout a pipeline wait recorded (cleared).
+int gemm_tc_poll_error();
+// Smallest token batch the model runtime sends to the tensor-core GEMM.
+constexpr int kTcMinTokens = 128;
+// x (Q8_F32 / Q8_BF16 / Q8_F16 rows) -> plain f16 rows [M][K].
+int to_f16_launch(const void* x, int dtype, int64_t ldx, int M, int K, __half* y, cudaStream_t st);
+
 int embed_launch(const void* packed_emb, int64_t d, const int32_t* ids, int64_t s, float* y,
                  cudaStream_t st);
-// y32 / yxs may be null; resid may be null.
+// y32 / yxs / y16 (plain f16 rows, the tensor-core GEMM input) may be null;
+// resid may be null.
 int rmsnorm_launch(float* x, const float* resid, const uint16_t* w, int64_t rows, int64_t d,
-                   float eps, float* y32, __half* yxs, cudaStream_t st);
+                   float eps, float* y32, __half* yxs, __half* y16, cudaStream_t st);
 int rmsnorm_heads_launch(const float* x, const uint16_t* w, int64_t rows, int64_t hd, float eps,
                          float* y, cudaStream_t st);
 int rope_kv_launch(float* qkv, int64_t ldqkv, int64_t T, const int32_t* pos, const int32_t* seq,
@@ -47,6 +62,7 @@ struct AttnArgs {
   float* part;                 // scratch: nqb*nkv*nsplit*(rmax*hd + 2*rmax) floats
   float* out32; int64_t ldo;   // nullable
   __half* outxs;               // nullable, XS over K = nh*hd
+  __half* out16;               // nullable, plain f16 rows [T][nh*hd]
 };
 int attention_init();
 int attention_launch(const AttnArgs& a, cudaStream_t st);

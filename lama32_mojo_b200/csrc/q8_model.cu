@@ -178,6 +178,7 @@ struct q8_ctx {
   float *h = nullptr, *qkv = nullptr, *ypart = nullptr, *logits = nullptr, *part = nullptr;
   size_t part_floats = 0;
   __half *xs_in = nullptr, *xs_ao = nullptr, *xs_act = nullptr;
+  bool tc = false;  // tensor-core GEMM for prefill batches (every K a multiple of 512)
   float *xn32 = nullptr, *ao32 = nullptr, *act32 = nullptr;  // f32 copies of the GEMV inputs
   float *am_val = nullptr, *am_gval = nullptr, *lg_gather = nullptr;
   int32_t *am_idx = nullptr, *am_gidx = nullptr;
@@ -256,14 +257,25 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
   // small token batches fuse RMSNorm into the GEMV prologue (K = hidden fits
   // the shared-memory staging); large batches keep the standalone kernel
   const bool fuse_norm = H <= 6144 && T <= 64;
+  // prefill-sized batches run the tensor-core GEMM on f16 activation rows;
+  // the XS buffers double as those rows (they hold twice the elements)
+  const bool tc = c->tc && blocks && T >= kTcMinTokens;
+  __half* xn16 = c->xs_in;
+  __half* ao16 = c->xs_ao;
+  __half* act16 = c->xs_act;
   for (int L = 0; L < c->cfg.layers; ++L) {
     const LayerW& w = c->layers[L];
-    if (!pending && fuse_norm) {  // RMSNorm fused into the GEMV prologue
+    if (tc) {
+      PROF(c, "rmsnorm", (double)T * H * (pending ? 14.0 : 10.0),
+           rmsnorm_launch(c->h, pending, w.in_norm, T, H, c->cfg.eps, nullptr, nullptr, xn16, st));
+      PROF(c, "gemm_qkv", gemv_bytes(T, H, nqkv),
+           gemm_tc_launch(EPI_STORE, xn16, H, T, H, w.qkv, nqkv, c->qkv, nqkv, nullptr, 0, st));
+    } else if (!pending && fuse_norm) {  // RMSNorm fused into the GEMV prologue
       PROF(c, "gemv_qkv", gemv_bytes(T, H, nqkv),
            gemv_rms_launch(EPI_STORE, c->h, H, w.in_norm, c->cfg.eps, T, H, w.qkv, nqkv, c->qkv, nqkv, nullptr, st));
     } else {
       PROF(c, "rmsnorm", (double)T * H * (pending ? 16.0 : 8.0),
-           rmsnorm_launch(c->h, pending, w.in_norm, T, H, c->cfg.eps, c->xn32, c->xs_in, st));
+           rmsnorm_launch(c->h, pending, w.in_norm, T, H, c->cfg.eps, c->xn32, c->xs_in, nullptr, st));
       PROF(c, "gemv_qkv", gemv_bytes(T, H, nqkv),
            gemm_dispatch(EPI_STORE, c->xn32, H, c->xs_in, T, H, w.qkv, nqkv, c->qkv, nqkv, nullptr, st));
     }
@@ -279,6 +291,11 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
     a.qb_tok0 = blocks ? c->qb_tok0_d : nullptr; a.qb_len = blocks ? c->qb_len_d : nullptr;
     a.nqb = nqb; a.qb_max = qb_max; a.nsplit = nsplit; a.part = c->part;
     a.out32 = c->ao32; a.ldo = c->qd; a.outxs = c->xs_ao;
+    if (tc) {
+      a.out32 = nullptr;
+      a.outxs = nullptr;
+      a.out16 = ao16;
+    }
     if (blocks) {
       PROF(c, "attention", kv_bytes_hint / c->cfg.layers + (double)T * c->qd * 8.0, attention_launch(a, st));
     } else {
@@ -287,7 +304,15 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
                                    c->bt_d, c->max_pages, nsplit, c->part, c->ticket_d, c->ao32, c->qd,
                                    c->xs_ao, st));
     }
-    if (!tp) {
+    if (tc) {
+      PROF(c, "gemm_o", gemv_bytes(T, c->qd, H),
+           gemm_tc_launch(tp ? EPI_STORE : EPI_ADD, ao16, c->qd, T, c->qd, w.o, H, tp ? c->ypart : c->h, H, nullptr,
+                          0, st));
+      if (tp) {
+        PROF(c, "allreduce", (double)T * H * 4.0, allreduce(c, c->ypart, (size_t)T * H));
+        pending = c->ypart;
+      }
+    } else if (!tp) {
       PROF(c, "gemv_o", gemv_bytes(T, c->qd, H),
            gemm_dispatch(EPI_ADD, c->ao32, c->qd, c->xs_ao, T, c->qd, w.o, H, c->h, H, nullptr, st));
     } else {
@@ -296,13 +321,28 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
       PROF(c, "allreduce", (double)T * H * 4.0, allreduce(c, c->ypart, (size_t)T * H));
       pending = c->ypart;
     }
+    if (tc) {
+      PROF(c, "rmsnorm", (double)T * H * (pending ? 14.0 : 10.0),
+           rmsnorm_launch(c->h, pending, w.post_norm, T, H, c->cfg.eps, nullptr, nullptr, xn16, st));
+      PROF(c, "gemm_gateup", gemv_bytes(T, H, 2 * c->F),
+           gemm_tc_launch(EPI_SWIGLU, xn16, H, T, H, w.gu, c->F, nullptr, 0, act16, c->F, st));
+      pending = nullptr;
+      PROF(c, "gemm_down", gemv_bytes(T, c->F, H),
+           gemm_tc_launch(tp ? EPI_STORE : EPI_ADD, act16, c->F, T, c->F, w.down, H, tp ? c->ypart : c->h, H,
+                          nullptr, 0, st));
+      if (tp) {
+        PROF(c, "allreduce", (double)T * H * 4.0, allreduce(c, c->ypart, (size_t)T * H));
+        pending = c->ypart;
+      }
+      continue;
+    }
     if (!pending && fuse_norm) {
       PROF(c, "gemv_gateup", gemv_bytes(T, H, 2 * c->F),
            gemv_rms_launch(EPI_SWIGLU, c->h, H, w.post_norm, c->cfg.eps, T, H, w.gu, c->F, c->act32, c->F,
                            c->xs_act, st));
     } else {
       PROF(c, "rmsnorm", (double)T * H * (pending ? 16.0 : 8.0),
-           rmsnorm_launch(c->h, pending, w.post_norm, T, H, c->cfg.eps, c->xn32, c->xs_in, st));
+           rmsnorm_launch(c->h, pending, w.post_norm, T, H, c->cfg.eps, c->xn32, c->xs_in, nullptr, st));
       PROF(c, "gemv_gateup", gemv_bytes(T, H, 2 * c->F),
            gemm_dispatch(EPI_SWIGLU, c->xn32, H, c->xs_in, T, H, w.gu, c->F, c->act32, c->F, c->xs_act, st));
     }
@@ -326,7 +366,7 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
                          c->V_loc, nullptr, st));
   } else {
     PROF(c, "rmsnorm", (double)lrows * H * 8.0,
-         rmsnorm_launch(hrow, prow, c->final_norm, lrows, H, c->cfg.eps, c->xn32, c->xs_in, st));
+         rmsnorm_launch(hrow, prow, c->final_norm, lrows, H, c->cfg.eps, c->xn32, c->xs_in, nullptr, st));
     PROF(c, "gemv_lmhead", gemv_bytes(lrows, H, c->V_loc),
          gemm_dispatch(EPI_STORE, c->xn32, H, c->xs_in, lrows, H, c->lm_head, c->V_loc, c->logits, c->V_loc, nullptr,
                        st));
@@ -544,6 +584,11 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
   c->qd = c->nh * c->hd;
   c->kvd = c->nkv * c->hd;
   c->F = C.inter / tp_size;
+  {
+    // Q8_TC=0 keeps prefill on the GEMV kernels (A/B comparisons)
+    const char* e = getenv("Q8_TC");
+    c->tc = C.hidden % 512 == 0 && c->qd % 512 == 0 && c->F % 512 == 0 && !(e && e[0] == '0');
+  }
   c->V = C.vocab;
   c->V_loc = C.vocab / tp_size;
   c->V_off = tp_rank * c->V_loc;
@@ -1009,6 +1054,7 @@ static int forward_impl(q8_ctx* c, const int32_t* ids, int s, int seq, float* lo
     Q8_TRY(run_tokens(c, T, T > 1, nqb, c->qb_max, nsplit, T - 1, last ? 1 : 0, kv_read_bytes(c, lens)));
     // the pinned staging is rewritten next chunk: wait for the copies
     Q8_CUDA(cudaStreamSynchronize(c->st));
+    if (c->tc && T >= kTcMinTokens) Q8_TRY(gemm_tc_poll_error());
     c->n_cached[seq] += T;
     done += T;
   }
@@ -1052,10 +1098,11 @@ static int forward_hidden_impl(q8_ctx* c, const int32_t* ids, int s, int seq, in
   c->cfg.layers = saved;
   Q8_TRY(st);
   if (c->tp_size > 1) {  // fold the last row-parallel partial into the residual
-    Q8_TRY(rmsnorm_launch(c->h, c->ypart, c->final_norm, T, c->H, c->cfg.eps, nullptr, nullptr, c->st));
+    Q8_TRY(rmsnorm_launch(c->h, c->ypart, c->final_norm, T, c->H, c->cfg.eps, nullptr, nullptr, nullptr, c->st));
   }
   Q8_CUDA(cudaMemcpyAsync(out, c->h, (size_t)T * c->H * 4, cudaMemcpyDeviceToHost, c->st));
   Q8_CUDA(cudaStreamSynchronize(c->st));
+  if (c->tc && T >= kTcMinTokens) Q8_TRY(gemm_tc_poll_error());
   return Q8_OK;
 }
 

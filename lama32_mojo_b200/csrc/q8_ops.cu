@@ -38,7 +38,8 @@ int embed_launch(const void* emb, int64_t d, const int32_t* ids, int64_t s, floa
 // One CTA per row; outputs f32 and/or split-f16 (XS) for the next GEMV.
 __global__ void __launch_bounds__(256) k_rmsnorm(float* __restrict__ x, const float* __restrict__ resid,
                                                  const uint16_t* __restrict__ w, int64_t d, float eps,
-                                                 float* __restrict__ y32, __half* __restrict__ yxs) {
+                                                 float* __restrict__ y32, __half* __restrict__ yxs,
+                                                 __half* __restrict__ y16) {
   __shared__ float wsum[8];
   pdl_trigger();
   pdl_wait();
@@ -70,13 +71,15 @@ __global__ void __launch_bounds__(256) k_rmsnorm(float* __restrict__ x, const fl
       yxs[xs_index(r, k, d, 0)] = hi;
       yxs[xs_index(r, k, d, 1)] = lo;
     }
+    if (y16) y16[r * d + k] = __float2half_rn(v);
   }
 }
 
 int rmsnorm_launch(float* x, const float* resid, const uint16_t* w, int64_t rows, int64_t d, float eps,
-                   float* y32, __half* yxs, cudaStream_t st) {
+                   float* y32, __half* yxs, __half* y16, cudaStream_t st) {
   if (rows <= 0) return Q8_OK;
-  return launch_pdl("k_rmsnorm", k_rmsnorm, dim3((unsigned)rows), dim3(256), 0, st, x, resid, w, d, eps, y32, yxs);
+  return launch_pdl("k_rmsnorm", k_rmsnorm, dim3((unsigned)rows), dim3(256), 0, st, x, resid, w, d, eps, y32, yxs,
+                    y16);
 }
 
 // Per-head RMSNorm (Qwen3 QK-norm) — k_rmsnorm2_w (src/llama_common.mojo:228-270); warp per row.
@@ -218,6 +221,7 @@ __device__ __forceinline__ void write_out(const AttnArgs& a, int tok, int col, f
     a.outxs[xs_index(tok, col, K, 0)] = hi;
     a.outxs[xs_index(tok, col, K, 1)] = lo;
   }
+  if (a.out16) a.out16[(int64_t)tok * (a.nh * a.hd) + col] = __float2half_rn(v);
 }
 
 __device__ __forceinline__ void write_out_tok(float* out32, int64_t ldo, __half* outxs, int K, int tok, int col,
@@ -749,7 +753,7 @@ extern "C" int q8op_rmsnorm(float* x, const float* resid, const uint16_t* w_bf16
                             float eps, float* y, void* stream) {
   Q8_CHECK_ARG(x && w_bf16 && y && rows >= 0 && d > 0, "q8op_rmsnorm: bad argument");
   Q8_CHECK_ARG(!(resid && x == y), "q8op_rmsnorm: y may alias x only without resid");
-  return rmsnorm_launch(x, resid, w_bf16, rows, d, eps, y, nullptr, (cudaStream_t)stream);
+  return rmsnorm_launch(x, resid, w_bf16, rows, d, eps, y, nullptr, nullptr, (cudaStream_t)stream);
 }
 
 extern "C" int q8op_rmsnorm_heads(const float* x, const uint16_t* w_bf16, int64_t rows, int64_t hd, float eps,

@@ -143,3 +143,9 @@ def argmax(logits: torch.Tensor) -> torch.Tensor:
     check(lib().q8op_argmax(_p(logits), logits.shape[0], logits.shape[1], logits.stride(0), _p(out),
                             _stream(logits)))
     return out
+
+
+def device_status() -> None:
+    """Synchronize the current device and raise if a tensor-core GEMM's bounded
+    pipeline wait timed out since the last poll (q8_device_status)."""
+    check(lib().q8_device_status())

@@ -238,3 +238,32 @@ def test_large_prefill_chunk_and_wide_batch(cuda, cfgname):
         o.forward(ids if s == 0 else prompts[s])
         close(lg[s], o.forward([toks[s]]))
         assert int(am[s]) == int(np.argmax(lg[s]))
+
+
+def test_tc_prefill_vs_oracle(cuda):
+    """Prefill chunks of >= 128 tokens run the tensor-core GEMMs (tiny-llama-untied
+    has every K a multiple of 512): 300 tokens as chunks of 128, 128 and 44
+    (tensor core, tensor core, GEMV), then greedy decode; per-layer hidden
+    states of a 200-token chunk; all within the f32 oracle gate."""
+    cfgname = "tiny-llama-untied"
+    ocfg = O.PRESETS[cfgname]
+    ck = O.make_q8_checkpoint(ocfg)
+    orc = O.OracleModel(ocfg, ck)
+    ids = O.random_ids(ocfg, 300, seed=12)
+    ref = orc.forward(ids)
+    toks = [int(np.argmax(ref))]
+    for _ in range(4):
+        toks.append(orc.forward_argmax([toks[-1]]))
+    m = build(cfgname, maxlen=320, max_tokens=128)
+    close(m.forward(ids), ref)
+    got = [int(np.argmax(ref))]
+    for _ in range(4):
+        got.append(m.forward_argmax([got[-1]]))
+    assert got == toks
+    m.close()
+    m2 = build(cfgname, maxlen=256, max_tokens=256)
+    o2 = O.OracleModel(ocfg, ck)
+    o2.forward(ids[:200])
+    for L in (0, 2):
+        close(m2.forward_hidden(ids[:200], L), o2.trace[f"after_layer{L}"])
+    m2.close()
