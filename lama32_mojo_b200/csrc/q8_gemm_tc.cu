@@ -5,20 +5,23 @@
 // (src/llama_common.mojo:476):
 //   y[m, n] (+)= sum_k x16[m, k] * f16(q[n, k] * s[n, k/64])
 //
-// Tile: 128 weight rows (MMA M) x 128 tokens (MMA N), K in steps of 64 (one
-// quantization group).  Warp roles (192 threads):
+// Tile: 128 weight rows (MMA M) x BN tokens (MMA N, 128 or 256), K in steps
+// of 64 (one quantization group).  Warp roles (320 threads):
 //   warp 0     TMA producer: two int8 code boxes [64 rows x 64 B] (no swizzle)
-//              and the f16 activation box [128 tokens x 128 B] (128 B swizzle)
+//              and the f16 activation box [BN tokens x 128 B] (128 B swizzle)
 //              into a 4-stage ring; completion counted in bytes on full[s].
-//   warps 2-5  dequantize codes x f16 group scale -> f16 (one rounding of the
-//              exact product) into the K-major 128 B-swizzled layout the
-//              tensor core reads; fence to the async proxy; arrive conv[s].
-//   warp 1     allocates 128 TMEM columns; one lane issues 4 x
+//   warps 2-9  two groups of 4 converter warps, alternating k-tiles: dequantize
+//              codes x f16 group scale -> f16 (one rounding of the exact
+//              product) into the K-major 128 B-swizzled layout the tensor core
+//              reads; fence to the async proxy; arrive conv[s].  Group scales
+//              are fetched 8 k-tiles (one uint4 per row) ahead.
+//   warp 1     allocates BN TMEM columns; one lane issues 4 x
 //              tcgen05.mma.kind::f16 (K = 16 each, f32 accumulate in TMEM) per
 //              stage and commits the stage back to empty[s].
-// Epilogue (warps 2-5, each owning the 32 TMEM lanes = weight rows of its
-// quadrant): tcgen05.ld.32x32b, then store / accumulate y[token][row]
-// (consecutive lanes -> consecutive rows: coalesced).  SwiGLU tiles hold 64
+// Epilogue (warps 2-9; each owns the 32 TMEM lanes = weight rows of its
+// quadrant, the two groups split the token columns): tcgen05.ld.32x32b, then
+// store / accumulate y[token][row] (consecutive lanes -> consecutive rows:
+// coalesced).  SwiGLU tiles hold 64
 // gate rows in lanes 0-63 and the matching up rows in lanes 64-127; the up
 // quadrants hand their values to the gate quadrants through shared memory.
 //
@@ -33,13 +36,9 @@
 
 namespace q8 {
 
-constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 64, TC_S = 4;
-constexpr int TC_CODES = TC_BM * TC_BK;          // 8 KB int8
-constexpr int TC_A = TC_BM * TC_BK * 2;          // 16 KB f16, SW128
-constexpr int TC_B = TC_BN * TC_BK * 2;          // 16 KB f16, SW128
-constexpr int TC_STAGE = TC_A + TC_B + TC_CODES; // 40 KB: A and B stay 1024 B aligned
-constexpr int TC_SMEM = TC_S * TC_STAGE + 1024;  // + alignment slack
-static_assert(TC_STAGE % 1024 == 0, "stage must keep 1024 B alignment for SW128");
+constexpr int TC_BM = 128, TC_BK = 64;
+constexpr int TC_CODES = TC_BM * TC_BK;  // 8 KB int8
+constexpr int TC_A = TC_BM * TC_BK * 2;  // 16 KB f16, SW128
 
 struct TcParams {
   const uint8_t* W;  // packed rows (group scales read from here)
@@ -86,7 +85,8 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Named barrier of one 4-warp epilogue group (ids 1 and 2).
+__device__ __forceinline__ void epi_bar(int grp) { asm volatile("bar.sync %0, 128;" ::"r"(grp + 1) : "memory"); }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
@@ -121,26 +121,47 @@ __device__ __forceinline__ void dequant16(uint4 c, __half2 s2, uint32_t (&h)[8])
   }
 }
 
-template <int EPI>
-__global__ void __launch_bounds__(192, 1) k_gemm_q8_tc(const __grid_constant__ CUtensorMap tm_codes,
+// Shared-memory bytes of one pipeline stage and of the whole ring for a
+// token tile of BN.
+template <int BN>
+struct TcCfg {
+  static constexpr int B = BN * TC_BK * 2;           // f16 activation box, SW128
+  static constexpr int STAGE = TC_A + B + TC_CODES;  // A | B | codes
+  static constexpr int S = 4;
+  static constexpr int SMEM = S * STAGE + 1024;      // + alignment slack
+  static_assert(STAGE % 1024 == 0, "stage must keep 1024 B alignment for SW128");
+};
+
+// 8 group scales (one uint4 of a packed row's scale block) -> scale of k-tile
+// 2*jj + grp.  jj comes from an unrolled loop (resolved at compile time); grp
+// (0/1) picks the f16 in the word.
+__device__ __forceinline__ __half pick_scale(uint4 b, int jj, int grp) {
+  const uint32_t w = jj == 0 ? b.x : jj == 1 ? b.y : jj == 2 ? b.z : b.w;
+  return __ushort_as_half((unsigned short)(grp ? (w >> 16) : (w & 0xFFFFu)));
+}
+
+template <int EPI, int BN>
+__global__ void __launch_bounds__(320, 1) k_gemm_q8_tc(const __grid_constant__ CUtensorMap tm_codes,
                                                        const __grid_constant__ CUtensorMap tm_x, TcParams p) {
+  using Cfg = TcCfg<BN>;
+  constexpr int S = Cfg::S;
   extern __shared__ uint8_t smem_raw[];
   // 1024 B alignment of the shared-window address (the swizzle atom)
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  __shared__ __align__(8) uint64_t full[TC_S], conv[TC_S], empty[TC_S], accf;
+  __shared__ __align__(8) uint64_t full[S], conv[S], empty[S], accf;
   __shared__ uint32_t tmem_base;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // token tiles vary fastest: CTAs resident together share one weight tile
-  const int m0 = blockIdx.x * TC_BN;
+  const int m0 = blockIdx.x * BN;
   const int r0 = blockIdx.y * (EPI == EPI_SWIGLU ? TC_BM / 2 : TC_BM);  // first output row (pair)
   // weight rows of the two 64-row code boxes
   const int rowA = r0, rowB = (EPI == EPI_SWIGLU) ? p.N + r0 : r0 + 64;
-  const int nk = p.K / TC_BK;
+  const int nk = p.K / TC_BK;  // a multiple of 8
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < TC_S; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&conv[s], 4);  // one arrive per converter warp
+      mbar_init(&conv[s], 4);  // the 4 warps of the converter group that owns stage s
       mbar_init(&empty[s], 1);
     }
     mbar_init(&accf, 1);
@@ -148,7 +169,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_q8_tc(const __grid_constant__ C
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
-                 "r"(TC_BN)
+                 "r"(BN)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -161,29 +182,29 @@ __global__ void __launch_bounds__(192, 1) k_gemm_q8_tc(const __grid_constant__ C
     // ---------------- TMA producer
     if (lane == 0) {
       for (int kt = 0; kt < nk; ++kt) {
-        const int s = kt % TC_S;
-        const uint32_t ph = (kt / TC_S) & 1;
+        const int s = kt % S;
+        const uint32_t ph = (kt / S) & 1;
         mbar_wait(&empty[s], ph ^ 1);
-        uint8_t* st = smem + s * TC_STAGE;
-        mbar_arrive_expect_tx(&full[s], TC_CODES + TC_B);
-        tma_load_2d(st + TC_A + TC_B, &tm_codes, kt * TC_BK, rowA, &full[s]);
-        tma_load_2d(st + TC_A + TC_B + TC_CODES / 2, &tm_codes, kt * TC_BK, rowB, &full[s]);
+        uint8_t* st = smem + s * Cfg::STAGE;
+        mbar_arrive_expect_tx(&full[s], TC_CODES + Cfg::B);
+        tma_load_2d(st + TC_A + Cfg::B, &tm_codes, kt * TC_BK, rowA, &full[s]);
+        tma_load_2d(st + TC_A + Cfg::B + TC_CODES / 2, &tm_codes, kt * TC_BK, rowB, &full[s]);
         tma_load_2d(st + TC_A, &tm_x, kt * TC_BK, m0, &full[s]);
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer
     // instruction descriptor: f32 accumulate, A = B = f16, both K-major,
-    // N = 128 (bits 17-22: N >> 3), M = 128 (bits 24-28: M >> 4)
-    const uint32_t idesc = (1u << 4) | ((uint32_t)(TC_BN >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+    // N = BN (bits 17-22: N >> 3), M = 128 (bits 24-28: M >> 4)
+    const uint32_t idesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
     if (lane == 0) {
       for (int kt = 0; kt < nk; ++kt) {
-        const int s = kt % TC_S;
-        const uint32_t ph = (kt / TC_S) & 1;
+        const int s = kt % S;
+        const uint32_t ph = (kt / S) & 1;
         mbar_wait(&full[s], ph);
         mbar_wait(&conv[s], ph);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        uint8_t* st = smem + s * TC_STAGE;
+        uint8_t* st = smem + s * Cfg::STAGE;
         const uint64_t da = sw128_desc(st), db = sw128_desc(st + TC_A);
 #pragma unroll
         for (int k = 0; k < TC_BK / 16; ++k)  // K = 16 -> 32 B further inside the swizzle atom
@@ -193,10 +214,12 @@ __global__ void __launch_bounds__(192, 1) k_gemm_q8_tc(const __grid_constant__ C
       tc_commit(&accf);
     }
   } else {
-    // ---------------- converters (128 threads), then the epilogue
-    const int ct = threadIdx.x - 64;
+    // ---------------- converters: two groups of 4 warps; group g converts the
+    // k-tiles kt = g (mod 2), so each group has two MMA periods per tile
+    const int grp = (warp - 2) >> 2;
+    const int ct = threadIdx.x - 64 - 128 * grp;  // 0..127 within the group
     // item it of thread ct: A row (it*128 + ct) >> 2, 16-code chunk (it*128 + ct) & 3
-    const __half* srow[4];
+    const uint4* srow[4];
 #pragma unroll
     for (int it = 0; it < 4; ++it) {
       const int row = (it * 128 + ct) >> 2;
@@ -209,53 +232,76 @@ __global__ void __launch_bounds__(192, 1) k_gemm_q8_tc(const __grid_constant__ C
         n = r0 + row;
         ok = n < p.N;
       }
-      srow[it] = ok ? reinterpret_cast<const __half*>(p.W + (int64_t)n * p.rb) : nullptr;
+      srow[it] = ok ? reinterpret_cast<const uint4*>(p.W + (int64_t)n * p.rb) : nullptr;
     }
-    for (int kt = 0; kt < nk; ++kt) {
-      const int s = kt % TC_S;
-      const uint32_t ph = (kt / TC_S) & 1;
-      __half sc[4];
+    const uint4 zero4 = make_uint4(0, 0, 0, 0);
+    uint4 snext[4];
 #pragma unroll
-      for (int it = 0; it < 4; ++it) sc[it] = srow[it] ? srow[it][kt] : __float2half(0.f);
-      mbar_wait(&full[s], ph);
-      uint8_t* st = smem + s * TC_STAGE;
-      const uint8_t* codes = st + TC_A + TC_B;
+    for (int it = 0; it < 4; ++it) snext[it] = srow[it] ? __ldg(srow[it]) : zero4;
+    for (int kb = 0; kb < nk / 8; ++kb) {
+      // scales of k-tiles 8kb..8kb+7 (one uint4 per row); fetch the next block
+      uint4 sblk[4];
 #pragma unroll
       for (int it = 0; it < 4; ++it) {
-        const int idx = it * 128 + ct;
-        const int row = idx >> 2, chunk = idx & 3;
-        uint32_t h[8];
-        dequant16(*reinterpret_cast<const uint4*>(codes + row * TC_BK + chunk * 16), __halves2half2(sc[it], sc[it]),
-                  h);
-        // 16 f16 = logical 16-byte chunks 2*chunk and 2*chunk+1 of the 128 B row
-        uint8_t* arow = st + row * 128;
-        *reinterpret_cast<uint4*>(arow + (((2 * chunk) ^ (row & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<uint4*>(arow + (((2 * chunk + 1) ^ (row & 7)) << 4)) = make_uint4(h[4], h[5], h[6], h[7]);
+        sblk[it] = snext[it];
+        snext[it] = (srow[it] && kb + 1 < nk / 8) ? __ldg(srow[it] + kb + 1) : zero4;
       }
-      fence_async_shared();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&conv[s]);
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const int kt = 8 * kb + 2 * jj + grp;
+        const int s = kt % S;
+        const uint32_t ph = (kt / S) & 1;
+        __half sc[4];
+#pragma unroll
+        for (int it = 0; it < 4; ++it) sc[it] = pick_scale(sblk[it], jj, grp);
+        mbar_wait(&full[s], ph);
+        uint8_t* st = smem + s * Cfg::STAGE;
+        const uint8_t* codes = st + TC_A + Cfg::B;
+        uint4 c[4];
+#pragma unroll
+        for (int it = 0; it < 4; ++it) {
+          const int idx = it * 128 + ct;
+          c[it] = *reinterpret_cast<const uint4*>(codes + (idx >> 2) * TC_BK + (idx & 3) * 16);
+        }
+#pragma unroll
+        for (int it = 0; it < 4; ++it) {
+          const int idx = it * 128 + ct;
+          const int row = idx >> 2, chunk = idx & 3;
+          uint32_t h[8];
+          dequant16(c[it], __halves2half2(sc[it], sc[it]), h);
+          // 16 f16 = logical 16-byte chunks 2*chunk and 2*chunk+1 of the 128 B row
+          uint8_t* arow = st + row * 128;
+          *reinterpret_cast<uint4*>(arow + (((2 * chunk) ^ (row & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+          *reinterpret_cast<uint4*>(arow + (((2 * chunk + 1) ^ (row & 7)) << 4)) =
+              make_uint4(h[4], h[5], h[6], h[7]);
+        }
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[s]);
+      }
     }
-    // ---------------- epilogue: this warp's TMEM lanes are A rows 32q..32q+31
+    // ---------------- epilogue: this warp's TMEM lanes are A rows 32q..32q+31;
+    // group g stores token columns [g*BN/2, (g+1)*BN/2)
     mbar_wait(&accf, 0);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const int q = warp & 3;
     const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16);
+    const int cbeg = grp * (BN / 2), cend = cbeg + BN / 2;
     if constexpr (EPI == EPI_SWIGLU) {
       // every MMA has completed: stage memory is free for the hand-off
-      float* xch = reinterpret_cast<float*>(smem);  // [64 rows][33]
+      float* xch = reinterpret_cast<float*>(smem) + grp * (64 * 33);  // [64 rows][33] per group
       const int pr = r0 + 32 * (q & 1) + lane;
 #pragma unroll 1
-      for (int c0 = 0; c0 < TC_BN; c0 += 32) {
+      for (int c0 = cbeg; c0 < cend; c0 += 32) {
         float v[32];
         tmem_ld32(tq + (uint32_t)c0, v);
         if (q >= 2) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) xch[(32 * (q - 2) + lane) * 33 + j] = v[j];
         }
-        epi_bar();
+        epi_bar(grp);
         if (q < 2 && pr < p.N) {
-#pragma unroll 4
+#pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int m = m0 + c0 + j;
             if (m < p.M) {
@@ -265,16 +311,16 @@ __global__ void __launch_bounds__(192, 1) k_gemm_q8_tc(const __grid_constant__ C
             }
           }
         }
-        epi_bar();
+        epi_bar(grp);
       }
     } else {
       const int n = r0 + 32 * q + lane;
 #pragma unroll 1
-      for (int c0 = 0; c0 < TC_BN; c0 += 32) {
+      for (int c0 = cbeg; c0 < cend; c0 += 32) {
         float v[32];
         tmem_ld32(tq + (uint32_t)c0, v);
         if (n < p.N) {
-#pragma unroll 4
+#pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int m = m0 + c0 + j;
             if (m < p.M) {
@@ -291,7 +337,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_q8_tc(const __grid_constant__ C
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_BN) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
   }
 }
 
@@ -315,6 +361,13 @@ static PFN_encodeTiled_t encode_fn() {
   return fn;
 }
 
+template <int EPI, int BN>
+static int tc_attr() {
+  Q8_CUDA(cudaFuncSetAttribute(k_gemm_q8_tc<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               TcCfg<BN>::SMEM));
+  return Q8_OK;
+}
+
 static int tc_init() {
   static bool done[64] = {false};
   static std::mutex mu;
@@ -322,11 +375,23 @@ static int tc_init() {
   Q8_CUDA(cudaGetDevice(&dev));
   std::lock_guard<std::mutex> lk(mu);
   if (done[dev & 63]) return Q8_OK;
-  Q8_CUDA(cudaFuncSetAttribute(k_gemm_q8_tc<EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
-  Q8_CUDA(cudaFuncSetAttribute(k_gemm_q8_tc<EPI_ADD>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
-  Q8_CUDA(cudaFuncSetAttribute(k_gemm_q8_tc<EPI_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
+  Q8_TRY((tc_attr<EPI_STORE, 128>()));
+  Q8_TRY((tc_attr<EPI_ADD, 128>()));
+  Q8_TRY((tc_attr<EPI_SWIGLU, 128>()));
+  Q8_TRY((tc_attr<EPI_STORE, 256>()));
+  Q8_TRY((tc_attr<EPI_ADD, 256>()));
+  Q8_TRY((tc_attr<EPI_SWIGLU, 256>()));
   done[dev & 63] = true;
   return Q8_OK;
+}
+
+template <int BN>
+static void tc_launch(int epi, dim3 grid, const CUtensorMap& tmc, const CUtensorMap& tmx, const TcParams& p,
+                      cudaStream_t st) {
+  constexpr int sm = TcCfg<BN>::SMEM;
+  if (epi == EPI_STORE) k_gemm_q8_tc<EPI_STORE, BN><<<grid, 320, sm, st>>>(tmc, tmx, p);
+  else if (epi == EPI_ADD) k_gemm_q8_tc<EPI_ADD, BN><<<grid, 320, sm, st>>>(tmc, tmx, p);
+  else k_gemm_q8_tc<EPI_SWIGLU, BN><<<grid, 320, sm, st>>>(tmc, tmx, p);
 }
 
 bool gemm_tc_supported(int K, const void* W, const __half* x16, int64_t ld16) {
@@ -345,6 +410,8 @@ int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int M, int K, const
   PFN_encodeTiled_t enc = encode_fn();
   const int64_t rb = q8_row_bytes(K);
   const int wrows = epi == EPI_SWIGLU ? 2 * N : N;
+  // 256-token tiles halve the dequantization work per MMA; small batches keep 128
+  const int bn = M >= 256 ? 256 : 128;
   CUtensorMap tmc, tmx;
   {
     // codes of every row: K bytes after the K/32 bytes of f16 group scales
@@ -363,7 +430,7 @@ int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int M, int K, const
   {
     cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
     cuuint64_t strides[1] = {(cuuint64_t)(ld16 * 2)};
-    cuuint32_t box[2] = {TC_BK, TC_BN};
+    cuuint32_t box[2] = {TC_BK, (cuuint32_t)bn};
     cuuint32_t es[2] = {1, 1};
     CUresult r = enc(&tmx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)x16, dims, strides, box, es,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -374,10 +441,9 @@ int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int M, int K, const
     }
   }
   TcParams p{(const uint8_t*)W, rb, K, N, M, y, ldy, y16, ldy16};
-  dim3 grid(ceil_div(M, TC_BN), epi == EPI_SWIGLU ? ceil_div(N, TC_BM / 2) : ceil_div(N, TC_BM));
-  if (epi == EPI_STORE) k_gemm_q8_tc<EPI_STORE><<<grid, 192, TC_SMEM, st>>>(tmc, tmx, p);
-  else if (epi == EPI_ADD) k_gemm_q8_tc<EPI_ADD><<<grid, 192, TC_SMEM, st>>>(tmc, tmx, p);
-  else k_gemm_q8_tc<EPI_SWIGLU><<<grid, 192, TC_SMEM, st>>>(tmc, tmx, p);
+  dim3 grid(ceil_div(M, bn), epi == EPI_SWIGLU ? ceil_div(N, TC_BM / 2) : ceil_div(N, TC_BM));
+  if (bn == 256) tc_launch<256>(epi, grid, tmc, tmx, p, st);
+  else tc_launch<128>(epi, grid, tmc, tmx, p, st);
   return launch_check("k_gemm_q8_tc");
 }
 
