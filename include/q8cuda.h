@@ -191,7 +191,9 @@ int q8_nccl_unique_id(void* out128);
  * of a [n, m] weight (quantize.py output); Q8_BF16: bf16 [n, m] (2-D tensors are
  * quantized on the GPU by the packer, 1-D norm weights are stored as bf16).
  * rows/cols are the LOGICAL [n, m] shape.  data_on_device selects host/device
- * source.  Tensor-parallel slicing (column/row/vocab parallel) happens here. */
+ * source; device data may still be in flight on any of the caller's streams
+ * (the call synchronizes the device before reading it).  Tensor-parallel
+ * slicing (column/row/vocab parallel) happens here. */
 int q8_load_tensor(q8_ctx* ctx, const char* name, int dtype, int64_t rows, int64_t cols,
                    const void* data, int data_on_device);
 

@@ -267,3 +267,33 @@ def test_tc_prefill_vs_oracle(cuda):
     for L in (0, 2):
         close(m2.forward_hidden(ids[:200], L), o2.trace[f"after_layer{L}"])
     m2.close()
+
+
+@pytest.mark.parametrize("cfgname", ["tiny-llama", "tiny-qwen3", "tiny-llama-untied"])
+def test_persistent_decode_step_matches_per_op(cuda, cfgname, monkeypatch):
+    """The opt-in persistent decode step (one cooperative launch per step,
+    Q8_MK=1) against the per-op kernels on the same checkpoint: cached decode
+    logits, on-device generation and batched decode agree with the oracle
+    and with each other."""
+    ocfg = O.PRESETS[cfgname]
+    ck = O.make_q8_checkpoint(ocfg)
+    ids = O.random_ids(ocfg, 11, seed=21)
+    out = {}
+    for mk in ("0", "1"):
+        monkeypatch.setenv("Q8_MK", mk)
+        m = build(cfgname, maxlen=40, max_seqs=2)
+        m.forward(ids[:-1])
+        lg = m.forward([ids[-1]])
+        t = int(np.argmax(lg))
+        gen = m.generate([t], [0], 4)[:, 0].tolist()
+        m.forward(ids[:5], seq=1)
+        am, lgb = m.decode([3, 5], [0, 1], logits=True)
+        out[mk] = (lg, gen, lgb)
+        m.close()
+    o = O.OracleModel(ocfg, ck)
+    o.forward(ids[:-1])
+    close(out["1"][0], o.forward([ids[-1]]))
+    r = O.rel_l2(out["1"][0], out["0"][0])
+    assert r < 1e-5, r
+    assert out["1"][1] == out["0"][1]
+    assert O.rel_l2(out["1"][2], out["0"][2]) < 1e-5
