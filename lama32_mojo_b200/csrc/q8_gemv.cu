@@ -742,6 +742,8 @@ int gemv_rms_launch(int epi, const float* h, int64_t ldh, const uint16_t* nw, fl
   Q8_CHECK_ARG(K % Q8_QG == 0 && K > 0 && K <= kRmsMaxK && N > 0 && M > 0, "gemv_rms: bad shape M=%d K=%d", M, K);
   Q8_CHECK_ARG(epi != EPI_ADD, "gemv_rms: residual epilogue not supported");
   Q8_CHECK_ARG(((uintptr_t)h & 15) == 0 && (ldh % 4) == 0 && ((uintptr_t)nw & 7) == 0, "gemv_rms: alignment");
+  if (gemv_d_enabled() && ((uintptr_t)nw & 15) == 0 && gemv_d_supported(M, K, N, true, W))
+    return gemv_d_launch(epi, true, nullptr, 0, h, ldh, nw, eps, M, K, W, N, y, ldy, ys, st);
   Q8_TRY(gemv_init());
   GemvParams p{};
   p.M = M; p.K = K; p.W = (const uint8_t*)W; p.rb = q8_row_bytes(K);
@@ -768,6 +770,9 @@ int gemv_launch(int epi, const float* x32, int64_t ldx32, const __half* xs, int 
   Q8_CHECK_ARG(((uintptr_t)W & 1) == 0, "gemv: packed weights must be 2-byte aligned");
   Q8_CHECK_ARG(((uintptr_t)xs & 15) == 0 && ((uintptr_t)x32 & 7) == 0 && (ldx32 % 2) == 0,
                "gemv: activation alignment");
+  if (gemv_d_enabled() && x32 && ((uintptr_t)x32 & 15) == 0 && (ldx32 % 4) == 0 &&
+      gemv_d_supported(M, K, N, false, W))
+    return gemv_d_launch(epi, false, x32, ldx32, nullptr, 0, nullptr, 0.f, M, K, W, N, y, ldy, ys, st);
   Q8_TRY(gemv_init());
   GemvParams p{};
   p.xs = xs; p.M = M; p.K = K; p.W = (const uint8_t*)W; p.rb = q8_row_bytes(K);

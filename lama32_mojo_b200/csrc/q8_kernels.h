@@ -16,6 +16,14 @@ int gemv_rms_launch(int epi, const float* h, int64_t ldh, const uint16_t* nw, fl
 // the other covers the shape.
 int gemv_launch(int epi, const float* x32, int64_t ldx32, const __half* xs, int M, int K, const void* W, int N,
                 float* y, int64_t ldy, __half* ys, cudaStream_t st);
+// Digit GEMV (int8 tensor cores, 1-2 tokens, K % 256 == 0): x f32 rows, or
+// x = RMSNorm(h) * nw when rms.  gemv_d_prepare sizes its per-device scratch
+// outside stream capture.
+bool gemv_d_supported(int M, int K, int N, bool rms, const void* W);
+int gemv_d_prepare(int max_tiles);
+int gemv_d_launch(int epi, bool rms, const float* x, int64_t ldx, const float* h, int64_t ldh, const uint16_t* nw,
+                  float eps, int M, int K, const void* W, int N, float* y, int64_t ldy, __half* ys, cudaStream_t st);
+bool gemv_d_enabled();
 // Decode-shaped GEMMs (the GEMV kernels above); prefill-sized batches go to
 // gemm_tc_launch.
 int gemm_dispatch(int epi, const float* x32, int64_t ldx32, const __half* xs, int M, int K, const void* W, int N,

@@ -783,6 +783,11 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
   if (cudaMallocHost((void**)&c->pin, (size_t)T * 5 * 4) != cudaSuccess)
     return bail((set_error("cudaMallocHost failed"), Q8_ERR_OOM));
 
+  // digit GEMV scratch (split-tile partials, tickets): sized here, outside any
+  // stream capture
+  if ((s = gemv_d_prepare(std::max({ceil_div(c->qd + 2 * c->kvd, 16), ceil_div(H, 16), ceil_div(c->F, 8),
+                                    ceil_div(c->V_loc, 16)})))) return bail(s);
+
   // ---- persistent decode step (opt-in, Q8_MK=1): one GPU, hd 64/128,
   // <= MK_GMAX q heads per kv head, every K a multiple of 256
   {

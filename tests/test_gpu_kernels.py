@@ -80,7 +80,7 @@ def _weights(cuda, K, N, seed):
 
 
 @pytest.mark.parametrize("K,N", SHAPES)
-@pytest.mark.parametrize("M", [1, 8])
+@pytest.mark.parametrize("M", [1, 2, 8])
 def test_gemv_sweep_vs_oracle(cuda, K, N, M):
     p = _weights(cuda, K, N, K + N)
     x = torch.randn((M, K), generator=torch.Generator(device=cuda).manual_seed(2), device=cuda).to(torch.bfloat16)
@@ -182,7 +182,7 @@ def test_gemv_f32_input_strided(cuda):
     close(y, O.mm_q8(x.contiguous().cpu().numpy(), packed_np(p), K), rel=1e-5)
 
 
-@pytest.mark.parametrize("M", [1, 5, 16])
+@pytest.mark.parametrize("M", [1, 2, 5, 16])
 def test_swiglu_epilogue(cuda, M):
     K, F = 2048, 1000
     p = _weights(cuda, K, 2 * F, 4)
