@@ -65,14 +65,21 @@ struct GdParams {
   __half* ys;         // optional split-f16 copy of the SwiGLU output (K' = N)
   float* part;        // split-tile partials [T][GD_SL][16][GD_MB]
   int* ticket;        // [T], zero at rest
+  int aligned;        // CTA ranges of whole tiles (no tile is shared by CTAs)
 };
 
 // ------------------------------------------------------------------ unit ranges
+// Tile-aligned ranges (CTA c owns tiles [c T/G, (c+1) T/G)) keep every tile
+// inside one CTA; quad-balanced ranges split the units evenly and let tiles
+// straddle CTAs.
 __host__ __device__ inline int gd_cu0(int U, int c, int G) {
   return 4 * (int)(((unsigned)c * (unsigned)(U / 4)) / (unsigned)G);
 }
 __host__ __device__ inline int gd_cta_of(int U, int x, int G) {
   return (int)((((unsigned)(x / 4) + 1u) * (unsigned)G - 1u) / (unsigned)(U / 4));
+}
+__host__ __device__ inline int gd_range0(const GdParams& p, int c, int G) {
+  return p.aligned ? p.ng * (int)(((unsigned)c * (unsigned)p.T) / (unsigned)G) : gd_cu0(p.U, c, G);
 }
 __device__ __forceinline__ int gd_wu0(int w, int cu0, int ncu) {
   return cu0 + 4 * (int)(((unsigned)(ncu / 4) * (unsigned)w) / (unsigned)GD_WARPS);
@@ -366,7 +373,7 @@ __global__ void __launch_bounds__(GD_THREADS, 2) k_gemv_d(GdParams p) {
   const int G = gridDim.x, c = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ng = p.ng;
-  const int cu0 = gd_cu0(p.U, c, G), cu1 = gd_cu0(p.U, c + 1, G), ncu = cu1 - cu0;
+  const int cu0 = gd_range0(p, c, G), cu1 = gd_range0(p, c + 1, G), ncu = cu1 - cu0;
   int8_t* xq = reinterpret_cast<int8_t*>(smem);
   float* fcol = reinterpret_cast<float*>(smem + (((size_t)p.M * p.K * 3 + 15) & ~(size_t)15));
 
@@ -609,8 +616,17 @@ int gemv_d_launch(int epi, bool rms, const float* x, int64_t ldx, const float* h
     const char* e = getenv("Q8_GD_CTAS");  // CTAs per SM (1: the next kernel's CTAs can be co-resident)
     return e ? std::max(1, std::min(2, atoi(e))) : 2;
   }();
-  int G = std::min(per_sm * num_sms(), p.U / 4);
-  {
+  // Q8_GD_BALANCED=1: quad-balanced ranges with tiles shared by CTAs
+  static const bool balanced = getenv("Q8_GD_BALANCED") != nullptr;
+  int G;
+  if (!balanced) {
+    // whole tiles per CTA, equal counts: G = ceil(T / ceil(T / Gmax))
+    const int gmax = per_sm * num_sms();
+    const int k = ceil_div(p.T, gmax);
+    G = ceil_div(p.T, k);
+    p.aligned = 1;
+  } else {
+    G = std::min(per_sm * num_sms(), p.U / 4);
     // a tile may be shared by at most GD_SL CTAs (its partial slots): with at
     // least qmin quads per CTA a tile of qt quads spans <= ceil((qt-1)/qmin)+1
     const int qt = p.ng / 4, need = ceil_div(qt - 1, GD_SL - 1);

@@ -320,10 +320,12 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
       PROF(c, "gemv_qkv", gemv_bytes(T, H, nqkv),
            gemm_dispatch(EPI_STORE, c->xn32, H, c->xs_in, T, H, w.qkv, nqkv, c->qkv, nqkv, nullptr, st));
     }
-    PROF(c, "rope_kv", (double)T * (c->qd + 3.0 * c->kvd) * 8.0,
-         rope_kv_launch(c->qkv, nqkv, T, c->pos_d, c->seq_d, c->nh, c->nkv, c->hd, c->inv_freq_d, w.q_norm,
-                        w.k_norm, c->cfg.eps, c->kpool + (size_t)L * c->layer_kv,
-                        c->vpool + (size_t)L * c->layer_kv, c->page, c->bt_d, c->max_pages, st));
+    // decode: RoPE, QK-norm and the KV append run inside the attention kernel
+    if (blocks)
+      PROF(c, "rope_kv", (double)T * (c->qd + 3.0 * c->kvd) * 8.0,
+           rope_kv_launch(c->qkv, nqkv, T, c->pos_d, c->seq_d, c->nh, c->nkv, c->hd, c->inv_freq_d, w.q_norm,
+                          w.k_norm, c->cfg.eps, c->kpool + (size_t)L * c->layer_kv,
+                          c->vpool + (size_t)L * c->layer_kv, c->page, c->bt_d, c->max_pages, st));
     AttnArgs a{};
     a.q = c->qkv; a.ldq = nqkv; a.T = T; a.pos = c->pos_d; a.seq = c->seq_d;
     a.nh = c->nh; a.nkv = c->nkv; a.hd = c->hd;
@@ -340,10 +342,12 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
     if (blocks) {
       PROF(c, "attention", kv_bytes_hint / c->cfg.layers + (double)T * c->qd * 8.0, attention_launch(a, st));
     } else {
+      const AttnRope rope{c->inv_freq_d, w.q_norm, w.k_norm, c->cfg.eps, const_cast<float*>(a.kp),
+                          const_cast<float*>(a.vp)};
       PROF(c, "attention", kv_bytes_hint / c->cfg.layers + (double)T * c->qd * 8.0,
            attention_decode_launch(c->qkv, nqkv, T, c->pos_d, c->seq_d, c->nh, c->nkv, c->hd, a.kp, a.vp, c->page,
                                    c->bt_d, c->max_pages, nsplit, c->part, c->ticket_d, c->ao32, c->qd,
-                                   c->xs_ao, st));
+                                   c->xs_ao, st, &rope));
     }
     if (tc) {
       PROF(c, "gemm_o", gemv_bytes(T, c->qd, H),
@@ -783,6 +787,7 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
   if (cudaMallocHost((void**)&c->pin, (size_t)T * 5 * 4) != cudaSuccess)
     return bail((set_error("cudaMallocHost failed"), Q8_ERR_OOM));
 
+  if ((s = argmax_prepare())) return bail(s);
   // digit GEMV scratch (split-tile partials, tickets): sized here, outside any
   // stream capture
   if ((s = gemv_d_prepare(std::max({ceil_div(c->qd + 2 * c->kvd, 16), ceil_div(H, 16), ceil_div(c->F, 8),

@@ -6,6 +6,7 @@
 #include "q8_kernels.h"
 #include <algorithm>
 #include <math.h>
+#include <mutex>
 
 namespace q8 {
 
@@ -452,6 +453,15 @@ struct AttnDecArgs {
   int* ticket;      // [T*nkv], zero at rest
   float* out32; int64_t ldo;
   __half* outxs;
+  // fused RoPE + QK-norm + KV append (k_rope_qk_copy2): when inv_freq is set,
+  // q and the new k / v come un-rotated from the q|k|v rows and the CTA whose
+  // split holds the token's position writes the cache slot
+  const float* inv_freq;
+  const uint16_t* qn;
+  const uint16_t* kn;
+  float eps;
+  float* kw;
+  float* vw;
 };
 
 constexpr int ATTD_U = 4;            // keys per chunk (two chunks in flight per warp)
@@ -467,13 +477,13 @@ __device__ __forceinline__ void attd_load(const AttnDecArgs& a, const int32_t* b
     const int j = min(j0 + u, w_hi - 1);
     const int64_t off = (((int64_t)btr[j / a.page] * a.nkv + kvh) * a.page + (j % a.page)) * HD + lane * E;
     if constexpr (E == 4) {
-      const float4 k4 = __ldg(reinterpret_cast<const float4*>(a.kp + off));
-      const float4 v4 = __ldg(reinterpret_cast<const float4*>(a.vp + off));
+      const float4 k4 = __ldcg(reinterpret_cast<const float4*>(a.kp + off));
+      const float4 v4 = __ldcg(reinterpret_cast<const float4*>(a.vp + off));
       kr[u][0] = k4.x; kr[u][1] = k4.y; kr[u][2] = k4.z; kr[u][3] = k4.w;
       vr[u][0] = v4.x; vr[u][1] = v4.y; vr[u][2] = v4.z; vr[u][3] = v4.w;
     } else {
-      const float2 k2 = __ldg(reinterpret_cast<const float2*>(a.kp + off));
-      const float2 v2 = __ldg(reinterpret_cast<const float2*>(a.vp + off));
+      const float2 k2 = __ldcg(reinterpret_cast<const float2*>(a.kp + off));
+      const float2 v2 = __ldcg(reinterpret_cast<const float2*>(a.vp + off));
       kr[u][0] = k2.x; kr[u][1] = k2.y;
       vr[u][0] = v2.x; vr[u][1] = v2.y;
     }
@@ -538,6 +548,56 @@ __global__ void __launch_bounds__(ATTD_W * 32, 2) k_attn_decode(AttnDecArgs a) {
   const int wper = (k_hi - k_lo + ATTD_W - 1) / ATTD_W;
   const int w_lo = min(k_hi, k_lo + warp * wper), w_hi = min(k_hi, w_lo + wper);
   const float qscale = 1.4426950408889634f / sqrtf((float)HD);  // log2(e)/sqrt(hd): exp2 domain
+  const int32_t* btr = a.bt + (int64_t)a.seq[b] * a.max_pages;
+  __shared__ float s_q[GMAX][HD];
+  if (a.inv_freq) {
+    // k_rope_qk_copy2 (src/llama_common.mojo:299-342) with the QK-norm of
+    // k_rmsnorm2_w in front: lane l holds dims l + 32j, so each rotate-half
+    // pair (d, d + hd/2) stays in one lane
+    constexpr int J = HD / 32;
+    const int p = a.pos[b];
+    const bool own_new = p >= k_lo && p < k_hi;
+    if (warp < G || (warp == ATTD_W - 1 && own_new)) {
+      const bool is_q = warp < G;
+      const float* src = a.q + (int64_t)b * a.ldq + (is_q ? (int64_t)(kvh * G + warp) * HD : (int64_t)(a.nh + kvh) * HD);
+      float v[J];
+#pragma unroll
+      for (int j = 0; j < J; ++j) v[j] = src[lane + 32 * j];
+      const uint16_t* nw = is_q ? a.qn : a.kn;
+      if (nw) {
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < J; ++j) ss = fmaf(v[j], v[j], ss);
+        ss = warp_sum(ss);
+        const float inv = 1.0f / sqrtf(ss / (float)HD + a.eps);
+#pragma unroll
+        for (int j = 0; j < J; ++j) v[j] = bf16_bits_to_f32(nw[lane + 32 * j]) * v[j] * inv;
+      }
+      const float fp = (float)p;
+#pragma unroll
+      for (int j = 0; j < J / 2; ++j) {
+        float sn, cs;
+        sincosf(fp * a.inv_freq[lane + 32 * j], &sn, &cs);
+        const float x0 = v[j], x1 = v[j + J / 2];
+        v[j] = x0 * cs - x1 * sn;
+        v[j + J / 2] = x1 * cs + x0 * sn;
+      }
+      if (is_q) {
+#pragma unroll
+        for (int j = 0; j < J; ++j) s_q[warp][lane + 32 * j] = v[j];
+      } else {
+        const int64_t off = (((int64_t)btr[p / a.page] * a.nkv + kvh) * a.page + (p % a.page)) * HD;
+        const float* vsrc = a.q + (int64_t)b * a.ldq + (int64_t)(a.nh + a.nkv + kvh) * HD;
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+          a.kw[off + lane + 32 * j] = v[j];
+          a.vw[off + lane + 32 * j] = vsrc[lane + 32 * j];
+        }
+      }
+    }
+    __threadfence_block();
+    __syncthreads();
+  }
 
   float q[GMAX][E], o[GMAX][E], m[GMAX], l[GMAX];
 #pragma unroll
@@ -547,10 +607,12 @@ __global__ void __launch_bounds__(ATTD_W * 32, 2) k_attn_decode(AttnDecArgs a) {
 #pragma unroll
     for (int e = 0; e < E; ++e) {
       o[g][e] = 0.f;
-      q[g][e] = (g < G) ? a.q[(int64_t)b * a.ldq + (int64_t)(kvh * G + g) * HD + lane * E + e] * qscale : 0.f;
+      q[g][e] = (g < G) ? (a.inv_freq ? s_q[g][lane * E + e]
+                                      : a.q[(int64_t)b * a.ldq + (int64_t)(kvh * G + g) * HD + lane * E + e]) *
+                              qscale
+                        : 0.f;
     }
   }
-  const int32_t* btr = a.bt + (int64_t)a.seq[b] * a.max_pages;
   if (w_lo < w_hi) {
     float k0[ATTD_U][E], v0[ATTD_U][E], k1[ATTD_U][E], v1[ATTD_U][E];
     attd_load<E>(a, btr, kvh, w_lo, w_hi, lane, k0, v0);
@@ -664,12 +726,22 @@ size_t attention_decode_part_floats(int T, int nkv, int nsplit, int group, int h
 int attention_decode_launch(const float* q, int64_t ldq, int T, const int32_t* pos, const int32_t* seq, int nh,
                             int nkv, int hd, const float* kp, const float* vp, int page, const int32_t* bt,
                             int max_pages, int nsplit, float* part, int* ticket, float* out32, int64_t ldo,
-                            __half* outxs, cudaStream_t st) {
+                            __half* outxs, cudaStream_t st, const AttnRope* rope) {
   Q8_CHECK_ARG(nkv > 0 && nh % nkv == 0 && nh / nkv <= 8, "attention decode: GQA group must be <= 8");
   Q8_CHECK_ARG(nsplit >= 1 && nsplit <= ATTD_MAXSPLIT && (nsplit == 1 || (part && ticket)),
                "attention decode: bad split count %d", nsplit);
   if (T <= 0) return Q8_OK;
-  AttnDecArgs a{q, ldq, pos, seq, T, nh, nkv, kp, vp, page, bt, max_pages, nsplit, part, ticket, out32, ldo, outxs};
+  AttnDecArgs a{q, ldq, pos, seq, T, nh, nkv, kp, vp, page, bt, max_pages, nsplit, part, ticket, out32, ldo, outxs,
+                nullptr, nullptr, nullptr, 0.f, nullptr, nullptr};
+  if (rope) {
+    Q8_CHECK_ARG(rope->inv_freq && rope->kw == kp && rope->vw == vp, "attention decode: bad rope arguments");
+    a.inv_freq = rope->inv_freq;
+    a.qn = rope->qn;
+    a.kn = rope->kn;
+    a.eps = rope->eps;
+    a.kw = rope->kw;
+    a.vw = rope->vw;
+  }
   dim3 grid(T * nkv, nsplit);
   const bool g4 = nh / nkv <= 4;
   const dim3 blk(ATTD_W * 32);
@@ -732,8 +804,105 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ x, in
   }
 }
 
+// Wide rows (vocabulary logits): blocks reduce chunks of the row; the last
+// block to finish (ticket counter) merges the chunk winners in chunk order, so
+// the result is the lowest index of the maximum, as in k_argmax.
+constexpr int ARGMAX_MAXB = 64;
+constexpr int ARGMAX_MAXROWS = 4096;
+
+__device__ __forceinline__ void amax_merge(float& bv, int& bi, float ov, int oi) {
+  if (ov > bv || (ov == bv && oi < bi)) {
+    bv = ov;
+    bi = oi;
+  }
+}
+
+__global__ void __launch_bounds__(256) k_argmax_mb(const float* __restrict__ x, int64_t n, int64_t ld,
+                                                   int32_t* __restrict__ out, float* pv, int* pi, int* ticket) {
+  __shared__ float sv[8];
+  __shared__ int si[8];
+  __shared__ int s_last;
+  pdl_trigger();
+  pdl_wait();
+  const int r = blockIdx.y, nb = gridDim.x, b = blockIdx.x;
+  const int64_t chunk = ((n + nb - 1) / nb + 3) & ~(int64_t)3;
+  const int64_t lo = (int64_t)b * chunk, hi = min(n, lo + chunk);
+  const float* row = x + (int64_t)r * ld;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  // lo is a multiple of 4: with a 16-byte aligned row the chunk reads as float4
+  const int64_t n4 = ((((uintptr_t)row) & 15) == 0 && hi > lo) ? (hi - lo) / 4 : 0;
+  for (int64_t q = threadIdx.x; q < n4; q += blockDim.x) {
+    const int64_t i = lo + 4 * q;
+    const float4 v = *reinterpret_cast<const float4*>(row + i);
+    amax_merge(bv, bi, v.x, (int)i);
+    amax_merge(bv, bi, v.y, (int)i + 1);
+    amax_merge(bv, bi, v.z, (int)i + 2);
+    amax_merge(bv, bi, v.w, (int)i + 3);
+  }
+  for (int64_t j = lo + 4 * n4 + threadIdx.x; j < hi; j += blockDim.x) amax_merge(bv, bi, row[j], (int)j);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax_merge(bv, bi, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o));
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    sv[w] = bv;
+    si[w] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int k = 1; k < (int)(blockDim.x >> 5); ++k) amax_merge(bv, bi, sv[k], si[k]);
+    pv[r * ARGMAX_MAXB + b] = bv;
+    pi[r * ARGMAX_MAXB + b] = bi;
+    __threadfence();
+    s_last = atomicAdd(ticket + r, 1) == nb - 1;
+    __threadfence();
+  }
+  __syncthreads();
+  if (!s_last || threadIdx.x != 0) return;
+  float v = -INFINITY;
+  int ix = 0x7fffffff;
+  for (int k = 0; k < nb; ++k) amax_merge(v, ix, __ldcg(pv + r * ARGMAX_MAXB + k), __ldcg(pi + r * ARGMAX_MAXB + k));
+  out[r] = (ix == 0x7fffffff) ? 0 : ix;
+  ticket[r] = 0;  // ready for the next launch
+}
+
+struct ArgmaxScratch {
+  float* pv = nullptr;
+  int* pi = nullptr;
+  int* ticket = nullptr;
+};
+static ArgmaxScratch g_amax[64];
+static std::mutex g_amax_mu;
+
+// Allocated once per device, outside stream capture (model creation calls it).
+int argmax_prepare() {
+  int dev = 0;
+  Q8_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_amax_mu);
+  ArgmaxScratch& s = g_amax[dev & 63];
+  if (s.pv) return Q8_OK;
+  if (cudaMalloc(&s.pv, (size_t)ARGMAX_MAXROWS * ARGMAX_MAXB * 4) != cudaSuccess ||
+      cudaMalloc(&s.pi, (size_t)ARGMAX_MAXROWS * ARGMAX_MAXB * 4) != cudaSuccess ||
+      cudaMalloc(&s.ticket, (size_t)ARGMAX_MAXROWS * 4) != cudaSuccess ||
+      cudaMemset(s.ticket, 0, (size_t)ARGMAX_MAXROWS * 4) != cudaSuccess) {
+    cudaGetLastError();
+    set_error("argmax scratch allocation failed");
+    return Q8_ERR_OOM;
+  }
+  return Q8_OK;
+}
+
 int argmax_launch(const float* logits, int64_t rows, int64_t n, int64_t ld, int32_t* out, cudaStream_t st) {
   if (rows <= 0) return Q8_OK;
+  if (n >= 16384 && rows <= ARGMAX_MAXROWS) {
+    Q8_TRY(argmax_prepare());
+    int dev = 0;
+    Q8_CUDA(cudaGetDevice(&dev));
+    const ArgmaxScratch& s = g_amax[dev & 63];
+    const int nb = (int)std::min<int64_t>(ARGMAX_MAXB, (n + 4095) / 4096);
+    return launch_pdl("k_argmax_mb", k_argmax_mb, dim3(nb, (unsigned)rows), dim3(256), 0, st, logits, n, ld, out,
+                      s.pv, s.pi, s.ticket);
+  }
   return launch_pdl("k_argmax", k_argmax, dim3((unsigned)rows), dim3(1024), 0, st, logits, n, ld, out);
 }
 

@@ -303,3 +303,11 @@ def test_argmax_lowest_index_ties(cuda):
     x[2] = 0.0
     a = ops.argmax(x).cpu().numpy()
     assert a[0] == int(torch.argmax(x[0]).item()) and a[1] == 7 and a[2] == 0
+    # ragged width (chunks of the multi-block reduction end mid-vector) and
+    # rows that are not 16-byte aligned
+    y = torch.randn((3, 50003), device=cuda)
+    y[0, 50002] = 50.0
+    y[2, 16385] = 50.0
+    y[2, 33000] = 50.0
+    b = ops.argmax(y).cpu().numpy()
+    assert b[0] == 50002 and b[1] == int(torch.argmax(y[1]).item()) and b[2] == 16385
