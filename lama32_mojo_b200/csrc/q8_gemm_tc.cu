@@ -48,6 +48,7 @@ struct TcParams {
   int64_t ldy;
   __half* y16;       // SwiGLU only: f16 copy of the output [M][ld16]
   int64_t ld16;
+  int64_t y16lo;     // > 0: also the f16 remainder a - f16(a), at y16 + y16lo
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -105,7 +106,32 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 
 // 16 int8 codes (one uint4) times the f16 group scale -> 16 f16 values.
 // Bytes are biased to u8, placed as the low mantissa byte of 1024.0h and the
-// 1152.0h bias removed: exact integers q, then one rounding of q * s.
+// 1152.0h bias removed: exact integers q, then one rounding of q * s.  With
+// LO the rounding remainder q*s - f16(q*s) is produced too (one fused
+// multiply-add: exact whenever it is an f16 normal, i.e. hi + lo = q*s to
+// ~2^-22 relative for the scales of quantized weights).
+template <bool LO>
+__device__ __forceinline__ void dequant16x(uint4 c, __half2 s2, uint32_t (&h)[8], uint32_t (&l)[8]) {
+  const uint32_t w[4] = {c.x ^ 0x80808080u, c.y ^ 0x80808080u, c.z ^ 0x80808080u, c.w ^ 0x80808080u};
+  const uint32_t k1152 = 0x64806480u;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t lo = __byte_perm(w[j], 0x64646464u, 0x5140), hi = __byte_perm(w[j], 0x64646464u, 0x5342);
+    const __half2 qa = __hsub2(*reinterpret_cast<__half2*>(&lo), *reinterpret_cast<const __half2*>(&k1152));
+    const __half2 qb = __hsub2(*reinterpret_cast<__half2*>(&hi), *reinterpret_cast<const __half2*>(&k1152));
+    const __half2 a = __hmul2(qa, s2);
+    const __half2 b = __hmul2(qb, s2);
+    h[2 * j] = *reinterpret_cast<const uint32_t*>(&a);
+    h[2 * j + 1] = *reinterpret_cast<const uint32_t*>(&b);
+    if constexpr (LO) {
+      const __half2 ra = __hfma2(qa, s2, __hneg2(a));
+      const __half2 rb = __hfma2(qb, s2, __hneg2(b));
+      l[2 * j] = *reinterpret_cast<const uint32_t*>(&ra);
+      l[2 * j + 1] = *reinterpret_cast<const uint32_t*>(&rb);
+    }
+  }
+}
+
 __device__ __forceinline__ void dequant16(uint4 c, __half2 s2, uint32_t (&h)[8]) {
   const uint32_t w[4] = {c.x ^ 0x80808080u, c.y ^ 0x80808080u, c.z ^ 0x80808080u, c.w ^ 0x80808080u};
   const uint32_t k1152 = 0x64806480u;
@@ -123,13 +149,17 @@ __device__ __forceinline__ void dequant16(uint4 c, __half2 s2, uint32_t (&h)[8])
 
 // Shared-memory bytes of one pipeline stage and of the whole ring for a
 // token tile of BN.
-template <int BN>
+// X (split operands): A and B each hold a hi and a lo tile.
+template <int BN, bool X>
 struct TcCfg {
-  static constexpr int B = BN * TC_BK * 2;           // f16 activation box, SW128
-  static constexpr int STAGE = TC_A + B + TC_CODES;  // A | B | codes
-  static constexpr int S = 4;
+  static constexpr int A = TC_A * (X ? 2 : 1);       // f16 weight tiles, SW128
+  static constexpr int B1 = BN * TC_BK * 2;          // one f16 activation box, SW128
+  static constexpr int B = B1 * (X ? 2 : 1);
+  static constexpr int STAGE = A + B + TC_CODES;     // A | B | codes
+  static constexpr int S = X ? (BN == 256 ? 2 : 3) : 4;
   static constexpr int SMEM = S * STAGE + 1024;      // + alignment slack
   static_assert(STAGE % 1024 == 0, "stage must keep 1024 B alignment for SW128");
+  static_assert(SMEM <= 227 * 1024, "ring exceeds shared memory");
 };
 
 // 8 group scales (one uint4 of a packed row's scale block) -> scale of k-tile
@@ -140,10 +170,11 @@ __device__ __forceinline__ __half pick_scale(uint4 b, int jj, int grp) {
   return __ushort_as_half((unsigned short)(grp ? (w >> 16) : (w & 0xFFFFu)));
 }
 
-template <int EPI, int BN>
+template <int EPI, int BN, bool X>
 __global__ void __launch_bounds__(320, 1) k_gemm_q8_tc(const __grid_constant__ CUtensorMap tm_codes,
-                                                       const __grid_constant__ CUtensorMap tm_x, TcParams p) {
-  using Cfg = TcCfg<BN>;
+                                                       const __grid_constant__ CUtensorMap tm_x,
+                                                       const __grid_constant__ CUtensorMap tm_xlo, TcParams p) {
+  using Cfg = TcCfg<BN, X>;
   constexpr int S = Cfg::S;
   extern __shared__ uint8_t smem_raw[];
   // 1024 B alignment of the shared-window address (the swizzle atom)
@@ -187,9 +218,10 @@ __global__ void __launch_bounds__(320, 1) k_gemm_q8_tc(const __grid_constant__ C
         mbar_wait(&empty[s], ph ^ 1);
         uint8_t* st = smem + s * Cfg::STAGE;
         mbar_arrive_expect_tx(&full[s], TC_CODES + Cfg::B);
-        tma_load_2d(st + TC_A + Cfg::B, &tm_codes, kt * TC_BK, rowA, &full[s]);
-        tma_load_2d(st + TC_A + Cfg::B + TC_CODES / 2, &tm_codes, kt * TC_BK, rowB, &full[s]);
-        tma_load_2d(st + TC_A, &tm_x, kt * TC_BK, m0, &full[s]);
+        tma_load_2d(st + Cfg::A + Cfg::B, &tm_codes, kt * TC_BK, rowA, &full[s]);
+        tma_load_2d(st + Cfg::A + Cfg::B + TC_CODES / 2, &tm_codes, kt * TC_BK, rowB, &full[s]);
+        tma_load_2d(st + Cfg::A, &tm_x, kt * TC_BK, m0, &full[s]);
+        if constexpr (X) tma_load_2d(st + Cfg::A + Cfg::B1, &tm_xlo, kt * TC_BK, m0, &full[s]);
       }
     }
   } else if (warp == 1) {
@@ -205,10 +237,17 @@ __global__ void __launch_bounds__(320, 1) k_gemm_q8_tc(const __grid_constant__ C
         mbar_wait(&conv[s], ph);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         uint8_t* st = smem + s * Cfg::STAGE;
-        const uint64_t da = sw128_desc(st), db = sw128_desc(st + TC_A);
+        const uint64_t da = sw128_desc(st), db = sw128_desc(st + Cfg::A);
 #pragma unroll
-        for (int k = 0; k < TC_BK / 16; ++k)  // K = 16 -> 32 B further inside the swizzle atom
+        for (int k = 0; k < TC_BK / 16; ++k) {  // K = 16 -> 32 B further inside the swizzle atom
           tc_mma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (kt | k) != 0);
+          if constexpr (X) {
+            // hi x lo and lo x hi; lo x lo is below the f32 accumulation error
+            const uint64_t dal = sw128_desc(st + TC_A), dbl = sw128_desc(st + Cfg::A + Cfg::B1);
+            tc_mma_f16(tmem, da + 2 * k, dbl + 2 * k, idesc, 1u);
+            tc_mma_f16(tmem, dal + 2 * k, db + 2 * k, idesc, 1u);
+          }
+        }
         tc_commit(&empty[s]);
       }
       tc_commit(&accf);
@@ -256,7 +295,7 @@ __global__ void __launch_bounds__(320, 1) k_gemm_q8_tc(const __grid_constant__ C
         for (int it = 0; it < 4; ++it) sc[it] = pick_scale(sblk[it], jj, grp);
         mbar_wait(&full[s], ph);
         uint8_t* st = smem + s * Cfg::STAGE;
-        const uint8_t* codes = st + TC_A + Cfg::B;
+        const uint8_t* codes = st + Cfg::A + Cfg::B;
         uint4 c[4];
 #pragma unroll
         for (int it = 0; it < 4; ++it) {
@@ -267,13 +306,17 @@ __global__ void __launch_bounds__(320, 1) k_gemm_q8_tc(const __grid_constant__ C
         for (int it = 0; it < 4; ++it) {
           const int idx = it * 128 + ct;
           const int row = idx >> 2, chunk = idx & 3;
-          uint32_t h[8];
-          dequant16(c[it], __halves2half2(sc[it], sc[it]), h);
+          uint32_t h[8], l[8];
+          dequant16x<X>(c[it], __halves2half2(sc[it], sc[it]), h, l);
           // 16 f16 = logical 16-byte chunks 2*chunk and 2*chunk+1 of the 128 B row
           uint8_t* arow = st + row * 128;
-          *reinterpret_cast<uint4*>(arow + (((2 * chunk) ^ (row & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
-          *reinterpret_cast<uint4*>(arow + (((2 * chunk + 1) ^ (row & 7)) << 4)) =
-              make_uint4(h[4], h[5], h[6], h[7]);
+          const int o0 = ((2 * chunk) ^ (row & 7)) << 4, o1 = ((2 * chunk + 1) ^ (row & 7)) << 4;
+          *reinterpret_cast<uint4*>(arow + o0) = make_uint4(h[0], h[1], h[2], h[3]);
+          *reinterpret_cast<uint4*>(arow + o1) = make_uint4(h[4], h[5], h[6], h[7]);
+          if constexpr (X) {
+            *reinterpret_cast<uint4*>(arow + TC_A + o0) = make_uint4(l[0], l[1], l[2], l[3]);
+            *reinterpret_cast<uint4*>(arow + TC_A + o1) = make_uint4(l[4], l[5], l[6], l[7]);
+          }
         }
         fence_async_shared();
         __syncwarp();
@@ -307,7 +350,11 @@ __global__ void __launch_bounds__(320, 1) k_gemm_q8_tc(const __grid_constant__ C
             if (m < p.M) {
               const float a = silu_mul(v[j], xch[(32 * q + lane) * 33 + j]);
               if (p.y) p.y[(int64_t)m * p.ldy + pr] = a;
-              if (p.y16) p.y16[(int64_t)m * p.ld16 + pr] = __float2half_rn(a);
+              if (p.y16) {
+                const __half hi = __float2half_rn(a);
+                p.y16[(int64_t)m * p.ld16 + pr] = hi;
+                if (p.y16lo) p.y16[p.y16lo + (int64_t)m * p.ld16 + pr] = __float2half_rn(a - __half2float(hi));
+              }
             }
           }
         }
@@ -320,14 +367,21 @@ __global__ void __launch_bounds__(320, 1) k_gemm_q8_tc(const __grid_constant__ C
         float v[32];
         tmem_ld32(tq + (uint32_t)c0, v);
         if (n < p.N) {
+          float* col = p.y + (int64_t)(m0 + c0) * p.ldy + n;
+          const int mcnt = min(32, p.M - (m0 + c0));
+          if constexpr (EPI == EPI_ADD) {
+            // all 32 residual reads in flight before the first store (the
+            // stores may alias them, so the compiler would serialize them)
+            float old[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int m = m0 + c0 + j;
-            if (m < p.M) {
-              float* dst = p.y + (int64_t)m * p.ldy + n;
-              if constexpr (EPI == EPI_ADD) *dst += v[j];
-              else *dst = v[j];
-            }
+            for (int j = 0; j < 32; ++j) old[j] = j < mcnt ? col[(int64_t)j * p.ldy] : 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < mcnt) col[(int64_t)j * p.ldy] = old[j] + v[j];
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < mcnt) col[(int64_t)j * p.ldy] = v[j];
           }
         }
       }
@@ -361,10 +415,21 @@ static PFN_encodeTiled_t encode_fn() {
   return fn;
 }
 
-template <int EPI, int BN>
+template <int EPI, int BN, bool X>
 static int tc_attr() {
-  Q8_CUDA(cudaFuncSetAttribute(k_gemm_q8_tc<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               TcCfg<BN>::SMEM));
+  Q8_CUDA(cudaFuncSetAttribute(k_gemm_q8_tc<EPI, BN, X>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               TcCfg<BN, X>::SMEM));
+  return Q8_OK;
+}
+
+template <bool X>
+static int tc_attr_all() {
+  Q8_TRY((tc_attr<EPI_STORE, 128, X>()));
+  Q8_TRY((tc_attr<EPI_ADD, 128, X>()));
+  Q8_TRY((tc_attr<EPI_SWIGLU, 128, X>()));
+  Q8_TRY((tc_attr<EPI_STORE, 256, X>()));
+  Q8_TRY((tc_attr<EPI_ADD, 256, X>()));
+  Q8_TRY((tc_attr<EPI_SWIGLU, 256, X>()));
   return Q8_OK;
 }
 
@@ -375,23 +440,19 @@ static int tc_init() {
   Q8_CUDA(cudaGetDevice(&dev));
   std::lock_guard<std::mutex> lk(mu);
   if (done[dev & 63]) return Q8_OK;
-  Q8_TRY((tc_attr<EPI_STORE, 128>()));
-  Q8_TRY((tc_attr<EPI_ADD, 128>()));
-  Q8_TRY((tc_attr<EPI_SWIGLU, 128>()));
-  Q8_TRY((tc_attr<EPI_STORE, 256>()));
-  Q8_TRY((tc_attr<EPI_ADD, 256>()));
-  Q8_TRY((tc_attr<EPI_SWIGLU, 256>()));
+  Q8_TRY(tc_attr_all<false>());
+  Q8_TRY(tc_attr_all<true>());
   done[dev & 63] = true;
   return Q8_OK;
 }
 
-template <int BN>
-static void tc_launch(int epi, dim3 grid, const CUtensorMap& tmc, const CUtensorMap& tmx, const TcParams& p,
-                      cudaStream_t st) {
-  constexpr int sm = TcCfg<BN>::SMEM;
-  if (epi == EPI_STORE) k_gemm_q8_tc<EPI_STORE, BN><<<grid, 320, sm, st>>>(tmc, tmx, p);
-  else if (epi == EPI_ADD) k_gemm_q8_tc<EPI_ADD, BN><<<grid, 320, sm, st>>>(tmc, tmx, p);
-  else k_gemm_q8_tc<EPI_SWIGLU, BN><<<grid, 320, sm, st>>>(tmc, tmx, p);
+template <int BN, bool X>
+static void tc_launch(int epi, dim3 grid, const CUtensorMap& tmc, const CUtensorMap& tmx, const CUtensorMap& tmxl,
+                      const TcParams& p, cudaStream_t st) {
+  constexpr int sm = TcCfg<BN, X>::SMEM;
+  if (epi == EPI_STORE) k_gemm_q8_tc<EPI_STORE, BN, X><<<grid, 320, sm, st>>>(tmc, tmx, tmxl, p);
+  else if (epi == EPI_ADD) k_gemm_q8_tc<EPI_ADD, BN, X><<<grid, 320, sm, st>>>(tmc, tmx, tmxl, p);
+  else k_gemm_q8_tc<EPI_SWIGLU, BN, X><<<grid, 320, sm, st>>>(tmc, tmx, tmxl, p);
 }
 
 bool gemm_tc_supported(int K, const void* W, const __half* x16, int64_t ld16) {
@@ -399,20 +460,48 @@ bool gemm_tc_supported(int K, const void* W, const __half* x16, int64_t ld16) {
          (ld16 * 2) % 16 == 0 && encode_fn() != nullptr;
 }
 
-int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int M, int K, const void* W, int N, float* y,
-                   int64_t ldy, __half* y16, int64_t ldy16, cudaStream_t st) {
+// Split operands (activation hi/lo planes, weight hi/lo tiles, three MMAs)
+// unless Q8_TC_FAST=1: single f16 operands, about 2^-12 relative per product.
+bool gemm_tc_exact() {
+  static const bool exact = [] {
+    const char* e = getenv("Q8_TC_FAST");
+    return !(e && e[0] == '1');
+  }();
+  return exact;
+}
+
+static int tc_x_map(PFN_encodeTiled_t enc, CUtensorMap* m, const __half* x16, int64_t ld16, int M, int K, int bn) {
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld16 * 2)};
+  cuuint32_t box[2] = {TC_BK, (cuuint32_t)bn};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)x16, dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("gemm_tc: activation tensor map encode failed (%d)", (int)r);
+    return Q8_ERR_CUDA;
+  }
+  return Q8_OK;
+}
+
+int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int64_t x16lo, int M, int K, const void* W, int N,
+                   float* y, int64_t ldy, __half* y16, int64_t ldy16, int64_t y16lo, cudaStream_t st) {
   if (M <= 0 || N <= 0) return Q8_OK;
   Q8_CHECK_ARG(gemm_tc_supported(K, W, x16, ld16),
                "gemm_tc: unsupported operands (K=%d must be a multiple of 512; 16-byte aligned W and x)", K);
   Q8_CHECK_ARG(epi == EPI_SWIGLU ? (y || y16) : y != nullptr, "gemm_tc: no output");
   Q8_CHECK_ARG(epi != EPI_SWIGLU || !y16 || (((uintptr_t)y16 & 1) == 0 && ldy16 >= N), "gemm_tc: bad y16");
+  Q8_CHECK_ARG(x16lo >= 0 && (x16lo * 2) % 16 == 0, "gemm_tc: lo plane must be 16-byte aligned");
   Q8_TRY(tc_init());
   PFN_encodeTiled_t enc = encode_fn();
   const int64_t rb = q8_row_bytes(K);
   const int wrows = epi == EPI_SWIGLU ? 2 * N : N;
-  // 256-token tiles halve the dequantization work per MMA; small batches keep 128
-  const int bn = M >= 256 ? 256 : 128;
-  CUtensorMap tmc, tmx;
+  const bool X = x16lo > 0;
+  // 256-token tiles halve the dequantization work per MMA (split operands
+  // keep 128: three ring stages instead of two)
+  const int bn = (!X && M >= 256) ? 256 : 128;
+  CUtensorMap tmc, tmx, tmxl;
   {
     // codes of every row: K bytes after the K/32 bytes of f16 group scales
     cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)wrows};
@@ -427,23 +516,13 @@ int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int M, int K, const
       return Q8_ERR_CUDA;
     }
   }
-  {
-    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
-    cuuint64_t strides[1] = {(cuuint64_t)(ld16 * 2)};
-    cuuint32_t box[2] = {TC_BK, (cuuint32_t)bn};
-    cuuint32_t es[2] = {1, 1};
-    CUresult r = enc(&tmx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)x16, dims, strides, box, es,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-      set_error("gemm_tc: activation tensor map encode failed (%d)", (int)r);
-      return Q8_ERR_CUDA;
-    }
-  }
-  TcParams p{(const uint8_t*)W, rb, K, N, M, y, ldy, y16, ldy16};
+  Q8_TRY(tc_x_map(enc, &tmx, x16, ld16, M, K, bn));
+  Q8_TRY(tc_x_map(enc, &tmxl, X ? x16 + x16lo : x16, ld16, M, K, bn));
+  TcParams p{(const uint8_t*)W, rb, K, N, M, y, ldy, y16, ldy16, y16lo};
   dim3 grid(ceil_div(M, bn), epi == EPI_SWIGLU ? ceil_div(N, TC_BM / 2) : ceil_div(N, TC_BM));
-  if (bn == 256) tc_launch<256>(epi, grid, tmc, tmx, p, st);
-  else tc_launch<128>(epi, grid, tmc, tmx, p, st);
+  if (X) tc_launch<128, true>(epi, grid, tmc, tmx, tmxl, p, st);
+  else if (bn == 256) tc_launch<256, false>(epi, grid, tmc, tmx, tmxl, p, st);
+  else tc_launch<128, false>(epi, grid, tmc, tmx, tmxl, p, st);
   return launch_check("k_gemm_q8_tc");
 }
 

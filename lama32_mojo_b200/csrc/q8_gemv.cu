@@ -561,25 +561,29 @@ int to_f32_launch(const void* x, int dtype, int64_t ldx, int M, int K, float* y,
   return launch_check("k_to_f32");
 }
 
-__global__ void k_to_f16(const void* __restrict__ x, int dtype, int64_t ldx, int M, int K, __half* __restrict__ y) {
+__global__ void k_to_f16(const void* __restrict__ x, int dtype, int64_t ldx, int M, int K, __half* __restrict__ y,
+                         int64_t ylo) {
   const int64_t total = (int64_t)M * K;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t m = i / K, k = i % K;
-    if (dtype == Q8_F16) {
+    if (dtype == Q8_F16) {  // exact in f16: the remainder is zero
       y[i] = reinterpret_cast<const __half*>(x)[m * ldx + k];
+      if (ylo) y[ylo + i] = __float2half_rn(0.f);
       continue;
     }
     const float v = dtype == Q8_F32 ? reinterpret_cast<const float*>(x)[m * ldx + k]
                                     : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[m * ldx + k]);
-    y[i] = __float2half_rn(v);
+    const __half hv = __float2half_rn(v);
+    y[i] = hv;
+    if (ylo) y[ylo + i] = __float2half_rn(v - __half2float(hv));
   }
 }
 
-int to_f16_launch(const void* x, int dtype, int64_t ldx, int M, int K, __half* y, cudaStream_t st) {
+int to_f16_launch(const void* x, int dtype, int64_t ldx, int M, int K, __half* y, cudaStream_t st, int64_t ylo) {
   const int64_t total = (int64_t)M * K;
   const int blocks = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 16);
-  k_to_f16<<<blocks, 256, 0, st>>>(x, dtype, ldx, M, K, y);
+  k_to_f16<<<blocks, 256, 0, st>>>(x, dtype, ldx, M, K, y, ylo);
   return launch_check("k_to_f16");
 }
 
@@ -845,10 +849,12 @@ static int op_gemm_common(int epi, const void* x, int x_dtype, int64_t ldx, int6
   cudaStream_t st = (cudaStream_t)stream;
   void* xs = nullptr;
   if (M >= kTcMinTokens && K % 512 == 0 && ((uintptr_t)w & 15) == 0) {
-    // prefill-sized batch: f16 rows -> tensor-core GEMM
-    Q8_TRY(op_scratch((size_t)M * K * 2, &xs));
-    Q8_TRY(to_f16_launch(x, x_dtype, ldx, (int)M, (int)K, (__half*)xs, st));
-    return gemm_tc_launch(epi, (const __half*)xs, K, (int)M, (int)K, w, (int)N, y, ldy, nullptr, 0, st);
+    // prefill-sized batch: f16 rows (split hi + lo unless fast mode) ->
+    // tensor-core GEMM
+    const int64_t lo = gemm_tc_exact() ? M * K : 0;
+    Q8_TRY(op_scratch((size_t)M * K * 4, &xs));
+    Q8_TRY(to_f16_launch(x, x_dtype, ldx, (int)M, (int)K, (__half*)xs, st, lo));
+    return gemm_tc_launch(epi, (const __half*)xs, K, lo, (int)M, (int)K, w, (int)N, y, ldy, nullptr, 0, 0, st);
   }
   Q8_TRY(op_scratch((size_t)M * K * 8, &xs));
   Q8_TRY(to_xs_launch(x, x_dtype, ldx, (int)M, (int)K, (__half*)xs, st));

@@ -33,22 +33,28 @@ int op_scratch(size_t bytes, void** out);
 // Tensor-core GEMM (tcgen05/TMEM) for prefill batches: x16 plain f16 rows
 // [M][ld16]; K a multiple of 512.  STORE/ADD write y (f32); SWIGLU (N = F
 // pairs, W = 2F rows gate|up) writes y and/or y16 (f16 rows [M][ldy16]).
+// x16lo > 0: the activations are split, lo = f16(x - f16(x)) at x16 + x16lo,
+// and the GEMM runs on split operands (exact to f32 accumulation); y16lo > 0
+// writes the SwiGLU output split the same way.  gemm_tc_exact(): whether
+// callers should produce split activations (Q8_TC_FAST=1 turns it off).
 bool gemm_tc_supported(int K, const void* W, const __half* x16, int64_t ld16);
-int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int M, int K, const void* W, int N, float* y,
-                   int64_t ldy, __half* y16, int64_t ldy16, cudaStream_t st);
+bool gemm_tc_exact();
+int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int64_t x16lo, int M, int K, const void* W, int N,
+                   float* y, int64_t ldy, __half* y16, int64_t ldy16, int64_t y16lo, cudaStream_t st);
 // After a synchronize: Q8_OK, or the timeout a pipeline wait recorded (cleared).
 int gemm_tc_poll_error();
 // Smallest token batch the model runtime sends to the tensor-core GEMM.
 constexpr int kTcMinTokens = 128;
 // x (Q8_F32 / Q8_BF16 / Q8_F16 rows) -> plain f16 rows [M][K].
-int to_f16_launch(const void* x, int dtype, int64_t ldx, int M, int K, __half* y, cudaStream_t st);
+int to_f16_launch(const void* x, int dtype, int64_t ldx, int M, int K, __half* y, cudaStream_t st,
+                  int64_t ylo = 0);
 
 int embed_launch(const void* packed_emb, int64_t d, const int32_t* ids, int64_t s, float* y,
                  cudaStream_t st);
 // y32 / yxs / y16 (plain f16 rows, the tensor-core GEMM input) may be null;
 // resid may be null.
 int rmsnorm_launch(float* x, const float* resid, const uint16_t* w, int64_t rows, int64_t d,
-                   float eps, float* y32, __half* yxs, __half* y16, cudaStream_t st);
+                   float eps, float* y32, __half* yxs, __half* y16, cudaStream_t st, int64_t y16lo = 0);
 int rmsnorm_heads_launch(const float* x, const uint16_t* w, int64_t rows, int64_t hd, float eps,
                          float* y, cudaStream_t st);
 int rope_kv_launch(float* qkv, int64_t ldqkv, int64_t T, const int32_t* pos, const int32_t* seq,
@@ -71,6 +77,7 @@ struct AttnArgs {
   float* out32; int64_t ldo;   // nullable
   __half* outxs;               // nullable, XS over K = nh*hd
   __half* out16;               // nullable, plain f16 rows [T][nh*hd]
+  int64_t out16lo;             // > 0: f16 remainder rows at out16 + out16lo
 };
 int attention_init();
 int attention_launch(const AttnArgs& a, cudaStream_t st);

@@ -304,13 +304,18 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
   __half* xn16 = c->xs_in;
   __half* ao16 = c->xs_ao;
   __half* act16 = c->xs_act;
+  // split activations: lo planes half a buffer further (each XS buffer holds
+  // max_tokens x 2K halves)
+  const bool tcx = tc && gemm_tc_exact();
+  const int64_t loH = tcx ? (int64_t)c->max_tokens * H : 0, loQ = tcx ? (int64_t)c->max_tokens * c->qd : 0,
+                loF = tcx ? (int64_t)c->max_tokens * c->F : 0;
   for (int L = 0; L < c->cfg.layers; ++L) {
     const LayerW& w = c->layers[L];
     if (tc) {
       PROF(c, "rmsnorm", (double)T * H * (pending ? 14.0 : 10.0),
-           rmsnorm_launch(c->h, pending, w.in_norm, T, H, c->cfg.eps, nullptr, nullptr, xn16, st));
+           rmsnorm_launch(c->h, pending, w.in_norm, T, H, c->cfg.eps, nullptr, nullptr, xn16, st, loH));
       PROF(c, "gemm_qkv", gemv_bytes(T, H, nqkv),
-           gemm_tc_launch(EPI_STORE, xn16, H, T, H, w.qkv, nqkv, c->qkv, nqkv, nullptr, 0, st));
+           gemm_tc_launch(EPI_STORE, xn16, H, loH, T, H, w.qkv, nqkv, c->qkv, nqkv, nullptr, 0, 0, st));
     } else if (!pending && fuse_norm) {  // RMSNorm fused into the GEMV prologue
       PROF(c, "gemv_qkv", gemv_bytes(T, H, nqkv),
            gemv_rms_launch(EPI_STORE, c->h, H, w.in_norm, c->cfg.eps, T, H, w.qkv, nqkv, c->qkv, nqkv, nullptr, st));
@@ -338,6 +343,7 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
       a.out32 = nullptr;
       a.outxs = nullptr;
       a.out16 = ao16;
+      a.out16lo = loQ;
     }
     if (blocks) {
       PROF(c, "attention", kv_bytes_hint / c->cfg.layers + (double)T * c->qd * 8.0, attention_launch(a, st));
@@ -351,8 +357,8 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
     }
     if (tc) {
       PROF(c, "gemm_o", gemv_bytes(T, c->qd, H),
-           gemm_tc_launch(tp ? EPI_STORE : EPI_ADD, ao16, c->qd, T, c->qd, w.o, H, tp ? c->ypart : c->h, H, nullptr,
-                          0, st));
+           gemm_tc_launch(tp ? EPI_STORE : EPI_ADD, ao16, c->qd, loQ, T, c->qd, w.o, H, tp ? c->ypart : c->h, H,
+                          nullptr, 0, 0, st));
       if (tp) {
         PROF(c, "allreduce", (double)T * H * 4.0, allreduce(c, c->ypart, (size_t)T * H));
         pending = c->ypart;
@@ -368,13 +374,13 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
     }
     if (tc) {
       PROF(c, "rmsnorm", (double)T * H * (pending ? 14.0 : 10.0),
-           rmsnorm_launch(c->h, pending, w.post_norm, T, H, c->cfg.eps, nullptr, nullptr, xn16, st));
+           rmsnorm_launch(c->h, pending, w.post_norm, T, H, c->cfg.eps, nullptr, nullptr, xn16, st, loH));
       PROF(c, "gemm_gateup", gemv_bytes(T, H, 2 * c->F),
-           gemm_tc_launch(EPI_SWIGLU, xn16, H, T, H, w.gu, c->F, nullptr, 0, act16, c->F, st));
+           gemm_tc_launch(EPI_SWIGLU, xn16, H, loH, T, H, w.gu, c->F, nullptr, 0, act16, c->F, loF, st));
       pending = nullptr;
       PROF(c, "gemm_down", gemv_bytes(T, c->F, H),
-           gemm_tc_launch(tp ? EPI_STORE : EPI_ADD, act16, c->F, T, c->F, w.down, H, tp ? c->ypart : c->h, H,
-                          nullptr, 0, st));
+           gemm_tc_launch(tp ? EPI_STORE : EPI_ADD, act16, c->F, loF, T, c->F, w.down, H, tp ? c->ypart : c->h, H,
+                          nullptr, 0, 0, st));
       if (tp) {
         PROF(c, "allreduce", (double)T * H * 4.0, allreduce(c, c->ypart, (size_t)T * H));
         pending = c->ypart;

@@ -40,7 +40,7 @@ int embed_launch(const void* emb, int64_t d, const int32_t* ids, int64_t s, floa
 __global__ void __launch_bounds__(256) k_rmsnorm(float* __restrict__ x, const float* __restrict__ resid,
                                                  const uint16_t* __restrict__ w, int64_t d, float eps,
                                                  float* __restrict__ y32, __half* __restrict__ yxs,
-                                                 __half* __restrict__ y16) {
+                                                 __half* __restrict__ y16, int64_t y16lo) {
   __shared__ float wsum[8];
   pdl_trigger();
   pdl_wait();
@@ -72,15 +72,19 @@ __global__ void __launch_bounds__(256) k_rmsnorm(float* __restrict__ x, const fl
       yxs[xs_index(r, k, d, 0)] = hi;
       yxs[xs_index(r, k, d, 1)] = lo;
     }
-    if (y16) y16[r * d + k] = __float2half_rn(v);
+    if (y16) {
+      const __half hv = __float2half_rn(v);
+      y16[r * d + k] = hv;
+      if (y16lo) y16[y16lo + r * d + k] = __float2half_rn(v - __half2float(hv));
+    }
   }
 }
 
 int rmsnorm_launch(float* x, const float* resid, const uint16_t* w, int64_t rows, int64_t d, float eps,
-                   float* y32, __half* yxs, __half* y16, cudaStream_t st) {
+                   float* y32, __half* yxs, __half* y16, cudaStream_t st, int64_t y16lo) {
   if (rows <= 0) return Q8_OK;
   return launch_pdl("k_rmsnorm", k_rmsnorm, dim3((unsigned)rows), dim3(256), 0, st, x, resid, w, d, eps, y32, yxs,
-                    y16);
+                    y16, y16lo);
 }
 
 // Per-head RMSNorm (Qwen3 QK-norm) — k_rmsnorm2_w (src/llama_common.mojo:228-270); warp per row.
@@ -222,7 +226,12 @@ __device__ __forceinline__ void write_out(const AttnArgs& a, int tok, int col, f
     a.outxs[xs_index(tok, col, K, 0)] = hi;
     a.outxs[xs_index(tok, col, K, 1)] = lo;
   }
-  if (a.out16) a.out16[(int64_t)tok * (a.nh * a.hd) + col] = __float2half_rn(v);
+  if (a.out16) {
+    const int64_t i = (int64_t)tok * (a.nh * a.hd) + col;
+    const __half hv = __float2half_rn(v);
+    a.out16[i] = hv;
+    if (a.out16lo) a.out16[a.out16lo + i] = __float2half_rn(v - __half2float(hv));
+  }
 }
 
 __device__ __forceinline__ void write_out_tok(float* out32, int64_t ldo, __half* outxs, int K, int tok, int col,

@@ -92,8 +92,8 @@ def test_gemv_sweep_vs_oracle(cuda, K, N, M):
 
 @pytest.mark.parametrize("M", [3, 64, 512])
 def test_gemm_larger_m_vs_oracle(cuda, M):
-    """M < 128: GEMV kernels (split-f16 activations, ~f32 accuracy); M >= 128
-    with K % 512 == 0: the tensor-core GEMM (f16 operands, f32 accumulate)."""
+    """M < 128: GEMV kernels; M >= 128 with K % 512 == 0: the tensor-core GEMM
+    on split operands.  Both carry f32 accuracy."""
     K, N = 2048, 512
     p = _weights(cuda, K, N, 11)
     x = torch.randn((M, K), device=cuda)
@@ -104,9 +104,9 @@ def test_gemm_larger_m_vs_oracle(cuda, M):
 
 def test_gemm_m4096_properties(cuda):
     """Full M=4096 of the sweep (tensor-core path): rows agree with the same
-    rows computed alone on the M=1 GEMV path within the f16-operand gate, the
-    product is linear under x -> 2x (exact in f16 except for subnormal
-    inputs), and rows do not depend on their position in the batch."""
+    rows computed alone on the M=1 GEMV path, the product is linear under
+    x -> 2x (power-of-two scaling is exact in the split operands except for
+    subnormals), and rows do not depend on their position in the batch."""
     K, N = 3072, 8192
     p = _weights(cuda, K, N, 5)
     x = torch.randn((4096, K), device=cuda)
@@ -122,18 +122,12 @@ def test_gemm_m4096_properties(cuda):
 
 
 # ------------------------------------------------------------------ tensor-core GEMM
-# The prefill GEMM feeds the tensor cores f16 operands: x rounded to f16 and
-# each weight as f16(q * s) (one rounding of the exact product), accumulated
-# in f32.  Against the f32 oracle that is ~2^-12 relative per operand; the
-# gate is the north-star 1e-3 relative L2.  Against a torch fp32 product of
-# the same f16-rounded operands only the summation order differs.
-TC_REL = 1e-3
-
-
-def _tc_ref(x: torch.Tensor, p: torch.Tensor, K: int) -> torch.Tensor:
-    w = torch.from_numpy(O.dequant_q8(packed_np(p), K)).to(x.device)
-    w16 = w.half().float()  # f32(q) * f32(s) is exact, so .half() is f16(q * s)
-    return x.half().float() @ w16.T
+# The prefill GEMM runs the tensor cores on split f16 operands: activations as
+# hi = f16(x) plus lo = f16(x - hi), weights as f16(q * s) plus its rounding
+# remainder, with hi*hi + hi*lo + lo*hi accumulated in f32.  That carries the
+# f32 arithmetic of the reference (W8A32) up to the f32 accumulation order, so
+# the gate against the f32 oracle is tight.
+TC_REL = 1e-4  # tensor-core f32 accumulation is not IEEE-exact (~1e-5 at K = 3072-14336)
 
 
 @pytest.mark.parametrize("M,K,N", [(128, 512, 128), (200, 1024, 200), (333, 4096, 384), (1000, 512, 72),
@@ -142,12 +136,8 @@ def test_tc_gemm_vs_oracle(cuda, M, K, N):
     p = _weights(cuda, K, N, M + K + N)
     x = torch.randn((M, K), generator=torch.Generator(device=cuda).manual_seed(M), device=cuda)
     y = ops.mm_q8(x, p, K)
-    r, _ = close(y.cpu().numpy(), O.mm_q8(x.cpu().numpy(), packed_np(p), K), rel=TC_REL)
+    close(y.cpu().numpy(), O.mm_q8(x.cpu().numpy(), packed_np(p), K), rel=TC_REL, mabs=1e-3)
     ops.device_status()
-    assert r < 6e-4
-    # accumulation differences only (order, and the tensor core's f32 adder):
-    # grows like sqrt(K)
-    close(y.cpu().numpy(), _tc_ref(x, p, K).cpu().numpy(), rel=3e-7 * np.sqrt(K), mabs=5e-4)
 
 
 @pytest.mark.parametrize("M,F", [(128, 512), (300, 200)])
@@ -158,9 +148,7 @@ def test_tc_swiglu_vs_oracle(cuda, M, F):
     y = ops.mm_q8_swiglu(x, p, K).cpu().numpy()
     ops.device_status()
     gu = O.mm_q8(x.float().cpu().numpy(), packed_np(p), K)
-    close(y, O.silu_mul(gu[:, :F], gu[:, F:]), rel=TC_REL)
-    gr = _tc_ref(x.float(), p, K).cpu().numpy()
-    close(y, O.silu_mul(gr[:, :F], gr[:, F:]), rel=5e-6, mabs=1e-4)
+    close(y, O.silu_mul(gu[:, :F], gu[:, F:]), rel=TC_REL, mabs=1e-3)
 
 
 @pytest.mark.parametrize("K,N", [(4096, 128256), (4096, 6144), (14336, 4096), (1792, 4096), (256, 1000),
