@@ -174,14 +174,25 @@ def main():
                        tp_rank=rank, tp_size=world, nccl_id=nid)
     rng = np.random.default_rng(1)
     first = []
+    ext = torch.cuda.ExternalStream(m.stream, device=dev)
+    # prompt prefill (tensor-core GEMMs for chunks of >= 128 tokens): timed with
+    # CUDA events, the last sequence's kernels profiled for the GEMM share
+    torch.cuda.synchronize()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    m.set_profiling(True)
+    p0.record(ext)
     for b in range(B):
         ids = rng.integers(0, cfg.vocab, size=prompt).tolist()
         lg = m.forward(ids, seq=b)
         if not np.isfinite(lg).all():
             raise SystemExit("prefill produced non-finite logits: the workload is invalid")
         first.append(int(np.argmax(lg)))
+    p1.record(ext)
+    torch.cuda.synchronize()
+    m.set_profiling(False)
+    prefill_ms = p0.elapsed_time(p1)
+    pprof = m.profile()
     seqs = list(range(B))
-    ext = torch.cuda.ExternalStream(m.stream, device=dev)
 
     def barrier():
         if world > 1:
@@ -268,6 +279,27 @@ def main():
     launches_per_step = sum(v[2] for v in agg.values()) // nprof + 1
     gpu_launches = launches_per_step * a.steps
 
+    # prefill summary: algorithmic GEMM flops (2*M*N*K; the split-operand mode
+    # issues three tensor-core MMAs per product) over the profiled GEMM time
+    H, F, L = cfg.hidden, cfg.inter // world, cfg.layers
+    qd, kvd = cfg.n_heads * cfg.head_dim // world, cfg.n_kv * cfg.head_dim // world
+    kn = {"gemm_qkv": H * (qd + 2 * kvd), "gemm_o": qd * H, "gemm_gateup": H * 2 * F, "gemm_down": F * H}
+    g_ms = sum(pprof[k][0] for k in kn if k in pprof)
+    g_fl = sum(2.0 * prompt * kn[k] * L for k in kn if k in pprof)
+    tot_ms = sum(v[0] for v in pprof.values())
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    tc_peak = float(peaks.get("bf16_tflops", 1590.0))
+    prefill = {"tokens": prompt * B, "ms": round(prefill_ms, 2), "tok_s": round(prompt * B / (prefill_ms / 1e3), 1),
+               "chunk_tokens": 2048,
+               "gemm_tflops": round(g_fl / (g_ms / 1e3) / 1e12, 1) if g_ms > 0 else None,
+               "gemm_peak_tflops": tc_peak, "gemm_frac": round(g_fl / (g_ms / 1e3) / 1e12 / tc_peak, 4) if g_ms > 0 else None,
+               "gemm_mode": "split operands (hi*hi + hi*lo + lo*hi tcgen05 MMAs, f32-accurate)",
+               "share": {k: round(v[0] / tot_ms, 3) for k, v in pprof.items()} if tot_ms > 0 else None}
+
     ctx_mid = prompt + a.warmup + a.steps // 2
     step_bytes = cfg.decode_bytes(B, ctx_mid, tp=world)
 
@@ -302,6 +334,7 @@ def main():
             "kernels": breakdown, "profiled_step_ms": round(step_ms_prof, 4),
             "gpu_launches": gpu_launches, "clocks": clk.summary(),
             "cpu_baseline": cpu,
+            "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
     m.close()
