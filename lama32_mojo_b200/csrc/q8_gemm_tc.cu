@@ -156,8 +156,12 @@ struct TcCfg {
   static constexpr int B1 = BN * TC_BK * 2;          // one f16 activation box, SW128
   static constexpr int B = B1 * (X ? 2 : 1);
   static constexpr int STAGE = A + B + TC_CODES;     // A | B | codes
-  static constexpr int S = X ? (BN == 256 ? 2 : 3) : 4;
+  // An even stage count: converter group g owns the stages of k-tiles kt = g
+  // (mod 2), so no group ever waits on a stage's mbarrier more than one phase
+  // ahead (a parity wait cannot tell phase r from phase r + 2).
+  static constexpr int S = X ? 2 : 4;
   static constexpr int SMEM = S * STAGE + 1024;      // + alignment slack
+  static_assert(S % 2 == 0, "converter groups alternate k-tiles: the ring needs an even stage count");
   static_assert(STAGE % 1024 == 0, "stage must keep 1024 B alignment for SW128");
   static_assert(SMEM <= 227 * 1024, "ring exceeds shared memory");
 };
@@ -498,9 +502,8 @@ int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int64_t x16lo, int 
   const int64_t rb = q8_row_bytes(K);
   const int wrows = epi == EPI_SWIGLU ? 2 * N : N;
   const bool X = x16lo > 0;
-  // 256-token tiles halve the dequantization work per MMA (split operands
-  // keep 128: three ring stages instead of two)
-  const int bn = (!X && M >= 256) ? 256 : 128;
+  // 256-token tiles halve the dequantization work per MMA
+  const int bn = M >= 256 ? 256 : 128;
   CUtensorMap tmc, tmx, tmxl;
   {
     // codes of every row: K bytes after the K/32 bytes of f16 group scales
@@ -520,7 +523,8 @@ int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int64_t x16lo, int 
   Q8_TRY(tc_x_map(enc, &tmxl, X ? x16 + x16lo : x16, ld16, M, K, bn));
   TcParams p{(const uint8_t*)W, rb, K, N, M, y, ldy, y16, ldy16, y16lo};
   dim3 grid(ceil_div(M, bn), epi == EPI_SWIGLU ? ceil_div(N, TC_BM / 2) : ceil_div(N, TC_BM));
-  if (X) tc_launch<128, true>(epi, grid, tmc, tmx, tmxl, p, st);
+  if (X && bn == 256) tc_launch<256, true>(epi, grid, tmc, tmx, tmxl, p, st);
+  else if (X) tc_launch<128, true>(epi, grid, tmc, tmx, tmxl, p, st);
   else if (bn == 256) tc_launch<256, false>(epi, grid, tmc, tmx, tmxl, p, st);
   else tc_launch<128, false>(epi, grid, tmc, tmx, tmxl, p, st);
   return launch_check("k_gemm_q8_tc");
