@@ -419,6 +419,29 @@ static PFN_encodeTiled_t encode_fn() {
   return fn;
 }
 
+// 2-D tensor map over `rows` rows of `inner` f32 elements, `row_bytes` apart
+// (the decode attention's K pool); box box_inner x box_rows, 128 B swizzle.
+int tensor_map_f32_rows(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t row_bytes,
+                        uint32_t box_inner, uint32_t box_rows) {
+  PFN_encodeTiled_t enc = encode_fn();
+  if (!enc) {
+    set_error("tensor map: cuTensorMapEncodeTiled unavailable");
+    return Q8_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("tensor map: encode failed (%d)", (int)r);
+    return Q8_ERR_CUDA;
+  }
+  return Q8_OK;
+}
+
 template <int EPI, int BN, bool X>
 static int tc_attr() {
   Q8_CUDA(cudaFuncSetAttribute(k_gemm_q8_tc<EPI, BN, X>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -544,5 +567,7 @@ int gemm_tc_poll_error() {
 
 extern "C" int q8_device_status(void) {
   Q8_CUDA(cudaDeviceSynchronize());
-  return q8::gemm_tc_poll_error();
+  const int a = q8::gemm_tc_poll_error();
+  const int b = q8::attn_dec_poll_error();
+  return a != 0 ? a : b;
 }

@@ -84,6 +84,9 @@ int attention_launch(const AttnArgs& a, cudaStream_t st);
 size_t attention_part_floats(int nqb, int nkv, int nsplit, int qb_max, int group, int hd);
 
 size_t attention_decode_part_floats(int T, int nkv, int nsplit, int group, int hd);
+// context splits for `items` (token, kv head) pairs: about one CTA per SM
+int attention_decode_nsplit(int items, int maxlen);
+int attn_dec_poll_error();
 // Fused RoPE / QK-norm / KV append for the decode attention: q and the new
 // k, v are read un-rotated from the q|k|v rows; kw / vw are the (same) pools.
 struct AttnRope {
@@ -97,7 +100,8 @@ struct AttnRope {
 int attention_decode_launch(const float* q, int64_t ldq, int T, const int32_t* pos, const int32_t* seq, int nh,
                             int nkv, int hd, const float* kp, const float* vp, int page, const int32_t* bt,
                             int max_pages, int nsplit, float* part, int* ticket, float* out32, int64_t ldo,
-                            __half* outxs, cudaStream_t st, const AttnRope* rope = nullptr);
+                            __half* outxs, cudaStream_t st, const AttnRope* rope = nullptr,
+                            int64_t pool_rows = 0);  // rows of each pool (0: unknown)
 
 int argmax_prepare();  // per-device scratch of the wide-row argmax (outside capture)
 int argmax_launch(const float* logits, int64_t rows, int64_t n, int64_t ld, int32_t* out,

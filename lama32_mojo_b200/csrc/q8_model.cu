@@ -353,7 +353,7 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
       PROF(c, "attention", kv_bytes_hint / c->cfg.layers + (double)T * c->qd * 8.0,
            attention_decode_launch(c->qkv, nqkv, T, c->pos_d, c->seq_d, c->nh, c->nkv, c->hd, a.kp, a.vp, c->page,
                                    c->bt_d, c->max_pages, nsplit, c->part, c->ticket_d, c->ao32, c->qd,
-                                   c->xs_ao, st, &rope));
+                                   c->xs_ao, st, &rope, (int64_t)(c->layer_kv / c->hd)));
     }
     if (tc) {
       PROF(c, "gemm_o", gemv_bytes(T, c->qd, H),
@@ -498,10 +498,7 @@ static int check_ready(q8_ctx* c) {
 
 static int decode_nsplit(q8_ctx* c, int B) {
   const int items = B * c->nkv;
-  int ns = ceil_div(2 * num_sms(), items);
-  ns = std::min(ns, ceil_div(c->maxlen, 128));
-  ns = std::min(ns, std::max(1, 1024 / items));
-  return std::max(1, ns);
+  return std::max(1, std::min(attention_decode_nsplit(items, c->maxlen), 1024 / items));
 }
 
 static double kv_read_bytes(q8_ctx* c, const std::vector<int>& ctxlens) {

@@ -441,327 +441,6 @@ int attention_launch(const AttnArgs& a, cudaStream_t st) {
   }
 }
 
-// ------------------------------------------------------------------ decode attention
-// One query token per sequence (the decode step).  CTA = (token b, kv head,
-// context split), 4 warps; each warp streams a contiguous run of keys of its
-// split, lanes own head_dim/32 consecutive dims, so every K and V row is one
-// coalesced 128-bit (hd 128) or 64-bit (hd 64) load per lane.  Keys are taken 8
-// at a time (16 row loads in flight per lane) with an online softmax over the
-// GQA group's G query heads held in registers (exp2 domain: q is pre-scaled by
-// log2(e)/sqrt(hd)).  Warps merge through shared memory; splits write
-// (o, m, l) partials and the last CTA of a (token, kv head) to finish merges
-// them (atomic ticket, reset by that CTA), so no combine launch is needed.
-struct AttnDecArgs {
-  const float* q; int64_t ldq;
-  const int32_t* pos; const int32_t* seq;
-  int T, nh, nkv;
-  const float* kp; const float* vp; int page;
-  const int32_t* bt; int max_pages;
-  int nsplit;
-  float* part;      // [T*nkv][nsplit][G*HD + 2G]
-  int* ticket;      // [T*nkv], zero at rest
-  float* out32; int64_t ldo;
-  __half* outxs;
-  // fused RoPE + QK-norm + KV append (k_rope_qk_copy2): when inv_freq is set,
-  // q and the new k / v come un-rotated from the q|k|v rows and the CTA whose
-  // split holds the token's position writes the cache slot
-  const float* inv_freq;
-  const uint16_t* qn;
-  const uint16_t* kn;
-  float eps;
-  float* kw;
-  float* vw;
-};
-
-constexpr int ATTD_U = 4;            // keys per chunk (two chunks in flight per warp)
-constexpr int ATTD_W = 8;            // warps per CTA
-constexpr int ATTD_MAXSPLIT = 128;   // context splits per (token, kv head)
-
-template <int E>
-__device__ __forceinline__ void attd_load(const AttnDecArgs& a, const int32_t* btr, int kvh, int j0, int w_hi,
-                                          int lane, float (&kr)[ATTD_U][E], float (&vr)[ATTD_U][E]) {
-  constexpr int HD = E * 32;
-#pragma unroll
-  for (int u = 0; u < ATTD_U; ++u) {
-    const int j = min(j0 + u, w_hi - 1);
-    const int64_t off = (((int64_t)btr[j / a.page] * a.nkv + kvh) * a.page + (j % a.page)) * HD + lane * E;
-    if constexpr (E == 4) {
-      const float4 k4 = __ldcg(reinterpret_cast<const float4*>(a.kp + off));
-      const float4 v4 = __ldcg(reinterpret_cast<const float4*>(a.vp + off));
-      kr[u][0] = k4.x; kr[u][1] = k4.y; kr[u][2] = k4.z; kr[u][3] = k4.w;
-      vr[u][0] = v4.x; vr[u][1] = v4.y; vr[u][2] = v4.z; vr[u][3] = v4.w;
-    } else {
-      const float2 k2 = __ldcg(reinterpret_cast<const float2*>(a.kp + off));
-      const float2 v2 = __ldcg(reinterpret_cast<const float2*>(a.vp + off));
-      kr[u][0] = k2.x; kr[u][1] = k2.y;
-      vr[u][0] = v2.x; vr[u][1] = v2.y;
-    }
-  }
-}
-
-// online-softmax update of the G heads with one chunk of ATTD_U keys (exp2 domain)
-template <int E, int GMAX>
-__device__ __forceinline__ void attd_chunk(int G, int j0, int w_hi, const float (&q)[GMAX][E],
-                                           const float (&kr)[ATTD_U][E], const float (&vr)[ATTD_U][E],
-                                           float (&o)[GMAX][E], float (&m)[GMAX], float (&l)[GMAX]) {
-#pragma unroll
-  for (int g = 0; g < GMAX; ++g) {
-    if (g >= G) break;
-    float sc[ATTD_U];
-#pragma unroll
-    for (int u = 0; u < ATTD_U; ++u) {
-      float d = 0.f;
-#pragma unroll
-      for (int e = 0; e < E; ++e) d = fmaf(q[g][e], kr[u][e], d);
-      sc[u] = d;
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-#pragma unroll
-      for (int u = 0; u < ATTD_U; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], off);
-    }
-    float mx = m[g];
-#pragma unroll
-    for (int u = 0; u < ATTD_U; ++u) {
-      if (j0 + u >= w_hi) sc[u] = -INFINITY;
-      mx = fmaxf(mx, sc[u]);
-    }
-    const float corr = (m[g] == -INFINITY) ? 0.f : exp2f(m[g] - mx);
-    float psum = 0.f;
-#pragma unroll
-    for (int e = 0; e < E; ++e) o[g][e] *= corr;
-#pragma unroll
-    for (int u = 0; u < ATTD_U; ++u) {
-      const float pz = (sc[u] == -INFINITY) ? 0.f : exp2f(sc[u] - mx);
-      psum += pz;
-#pragma unroll
-      for (int e = 0; e < E; ++e) o[g][e] = fmaf(pz, vr[u][e], o[g][e]);
-    }
-    l[g] = l[g] * corr + psum;
-    m[g] = mx;
-  }
-}
-
-template <int HD, int GMAX>
-__global__ void __launch_bounds__(ATTD_W * 32, 2) k_attn_decode(AttnDecArgs a) {
-  constexpr int E = HD / 32;
-  pdl_trigger();
-  pdl_wait();
-  const int item = blockIdx.x, sp = blockIdx.y;
-  const int b = item / a.nkv, kvh = item % a.nkv;
-  const int G = a.nh / a.nkv;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kv_end = a.pos[b] + 1;
-  const int per = (kv_end + a.nsplit - 1) / a.nsplit;
-  const int k_lo = min(kv_end, sp * per), k_hi = min(kv_end, k_lo + per);
-  const int wper = (k_hi - k_lo + ATTD_W - 1) / ATTD_W;
-  const int w_lo = min(k_hi, k_lo + warp * wper), w_hi = min(k_hi, w_lo + wper);
-  const float qscale = 1.4426950408889634f / sqrtf((float)HD);  // log2(e)/sqrt(hd): exp2 domain
-  const int32_t* btr = a.bt + (int64_t)a.seq[b] * a.max_pages;
-  __shared__ float s_q[GMAX][HD];
-  if (a.inv_freq) {
-    // k_rope_qk_copy2 (src/llama_common.mojo:299-342) with the QK-norm of
-    // k_rmsnorm2_w in front: lane l holds dims l + 32j, so each rotate-half
-    // pair (d, d + hd/2) stays in one lane
-    constexpr int J = HD / 32;
-    const int p = a.pos[b];
-    const bool own_new = p >= k_lo && p < k_hi;
-    if (warp < G || (warp == ATTD_W - 1 && own_new)) {
-      const bool is_q = warp < G;
-      const float* src = a.q + (int64_t)b * a.ldq + (is_q ? (int64_t)(kvh * G + warp) * HD : (int64_t)(a.nh + kvh) * HD);
-      float v[J];
-#pragma unroll
-      for (int j = 0; j < J; ++j) v[j] = src[lane + 32 * j];
-      const uint16_t* nw = is_q ? a.qn : a.kn;
-      if (nw) {
-        float ss = 0.f;
-#pragma unroll
-        for (int j = 0; j < J; ++j) ss = fmaf(v[j], v[j], ss);
-        ss = warp_sum(ss);
-        const float inv = 1.0f / sqrtf(ss / (float)HD + a.eps);
-#pragma unroll
-        for (int j = 0; j < J; ++j) v[j] = bf16_bits_to_f32(nw[lane + 32 * j]) * v[j] * inv;
-      }
-      const float fp = (float)p;
-#pragma unroll
-      for (int j = 0; j < J / 2; ++j) {
-        float sn, cs;
-        sincosf(fp * a.inv_freq[lane + 32 * j], &sn, &cs);
-        const float x0 = v[j], x1 = v[j + J / 2];
-        v[j] = x0 * cs - x1 * sn;
-        v[j + J / 2] = x1 * cs + x0 * sn;
-      }
-      if (is_q) {
-#pragma unroll
-        for (int j = 0; j < J; ++j) s_q[warp][lane + 32 * j] = v[j];
-      } else {
-        const int64_t off = (((int64_t)btr[p / a.page] * a.nkv + kvh) * a.page + (p % a.page)) * HD;
-        const float* vsrc = a.q + (int64_t)b * a.ldq + (int64_t)(a.nh + a.nkv + kvh) * HD;
-#pragma unroll
-        for (int j = 0; j < J; ++j) {
-          a.kw[off + lane + 32 * j] = v[j];
-          a.vw[off + lane + 32 * j] = vsrc[lane + 32 * j];
-        }
-      }
-    }
-    __threadfence_block();
-    __syncthreads();
-  }
-
-  float q[GMAX][E], o[GMAX][E], m[GMAX], l[GMAX];
-#pragma unroll
-  for (int g = 0; g < GMAX; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.f;
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-      o[g][e] = 0.f;
-      q[g][e] = (g < G) ? (a.inv_freq ? s_q[g][lane * E + e]
-                                      : a.q[(int64_t)b * a.ldq + (int64_t)(kvh * G + g) * HD + lane * E + e]) *
-                              qscale
-                        : 0.f;
-    }
-  }
-  if (w_lo < w_hi) {
-    float k0[ATTD_U][E], v0[ATTD_U][E], k1[ATTD_U][E], v1[ATTD_U][E];
-    attd_load<E>(a, btr, kvh, w_lo, w_hi, lane, k0, v0);
-    for (int j0 = w_lo; j0 < w_hi; j0 += 2 * ATTD_U) {
-      const int j1 = j0 + ATTD_U;
-      if (j1 < w_hi) attd_load<E>(a, btr, kvh, j1, w_hi, lane, k1, v1);
-      attd_chunk<E, GMAX>(G, j0, w_hi, q, k0, v0, o, m, l);
-      if (j1 < w_hi) {
-        if (j1 + ATTD_U < w_hi) attd_load<E>(a, btr, kvh, j1 + ATTD_U, w_hi, lane, k0, v0);
-        attd_chunk<E, GMAX>(G, j1, w_hi, q, k1, v1, o, m, l);
-      }
-    }
-  }
-
-  // merge the warps: (m, l, o) per head
-  __shared__ float sm_m[ATTD_W][GMAX], sm_l[ATTD_W][GMAX];
-  __shared__ float sm_o[ATTD_W][GMAX][HD];
-  __shared__ int s_last;
-  if (lane == 0) {
-#pragma unroll
-    for (int g = 0; g < GMAX; ++g) {
-      sm_m[warp][g] = m[g];
-      sm_l[warp][g] = l[g];
-    }
-  }
-#pragma unroll
-  for (int g = 0; g < GMAX; ++g) {
-    if (g >= G) break;
-#pragma unroll
-    for (int e = 0; e < E; ++e) sm_o[warp][g][lane * E + e] = o[g][e];
-  }
-  __syncthreads();
-  const int W = G * HD + 2 * G;
-  float* mypart = a.part + ((int64_t)item * a.nsplit + sp) * W;
-  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
-    const int g = i / HD, d = i % HD;
-    float M = -INFINITY;
-    for (int w = 0; w < ATTD_W; ++w) M = fmaxf(M, sm_m[w][g]);
-    float L = 0.f, O = 0.f;
-    if (M != -INFINITY) {
-      for (int w = 0; w < ATTD_W; ++w) {
-        if (sm_m[w][g] == -INFINITY) continue;
-        const float f = exp2f(sm_m[w][g] - M);
-        L = fmaf(sm_l[w][g], f, L);
-        O = fmaf(sm_o[w][g][d], f, O);
-      }
-    }
-    if (a.nsplit == 1) {
-      write_out_tok(a.out32, a.ldo, a.outxs, a.nh * HD, b, (kvh * G + g) * HD + d, L > 0.f ? O / L : 0.f);
-    } else {
-      mypart[i] = O;
-      if (d == 0) {
-        mypart[G * HD + g] = M;
-        mypart[G * HD + G + g] = L;
-      }
-    }
-  }
-  if (a.nsplit == 1) return;
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = (atomicAdd(&a.ticket[item], 1) == a.nsplit - 1);
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  // merge the splits: per-split weights exp2(m_s - M) once in shared memory,
-  // then each output sums the partials in rounds of 16 independent loads
-  const float* base = a.part + (int64_t)item * a.nsplit * W;
-  __shared__ float s_w[GMAX][ATTD_MAXSPLIT];
-  __shared__ float s_l[GMAX][ATTD_MAXSPLIT];
-  __shared__ float s_L[GMAX];
-  for (int idx = threadIdx.x; idx < G * a.nsplit; idx += blockDim.x) {
-    const int g = idx / a.nsplit, s2 = idx % a.nsplit;
-    s_w[g][s2] = __ldcg(base + (int64_t)s2 * W + G * HD + g);
-    s_l[g][s2] = __ldcg(base + (int64_t)s2 * W + G * HD + G + g);
-  }
-  __syncthreads();
-  if (threadIdx.x < G) {
-    const int g = threadIdx.x;
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < a.nsplit; ++s2) M = fmaxf(M, s_w[g][s2]);
-    float L = 0.f;
-    for (int s2 = 0; s2 < a.nsplit; ++s2) {
-      const float f = (M == -INFINITY || s_w[g][s2] == -INFINITY) ? 0.f : exp2f(s_w[g][s2] - M);
-      s_w[g][s2] = f;
-      L = fmaf(s_l[g][s2], f, L);
-    }
-    s_L[g] = L;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
-    const int g = i / HD, d = i % HD;
-    float O = 0.f;
-    for (int s0 = 0; s0 < a.nsplit; s0 += 16) {
-      float v[16];
-#pragma unroll
-      for (int u = 0; u < 16; ++u) v[u] = (s0 + u < a.nsplit) ? __ldcg(base + (int64_t)(s0 + u) * W + i) : 0.f;
-#pragma unroll
-      for (int u = 0; u < 16; ++u)
-        if (s0 + u < a.nsplit) O = fmaf(v[u], s_w[g][s0 + u], O);
-    }
-    const float L = s_L[g];
-    write_out_tok(a.out32, a.ldo, a.outxs, a.nh * HD, b, (kvh * G + g) * HD + d, L > 0.f ? O / L : 0.f);
-  }
-  if (threadIdx.x == 0) a.ticket[item] = 0;  // ready for the next launch
-}
-
-size_t attention_decode_part_floats(int T, int nkv, int nsplit, int group, int hd) {
-  return (size_t)T * nkv * nsplit * (size_t)(group * hd + 2 * group);
-}
-
-int attention_decode_launch(const float* q, int64_t ldq, int T, const int32_t* pos, const int32_t* seq, int nh,
-                            int nkv, int hd, const float* kp, const float* vp, int page, const int32_t* bt,
-                            int max_pages, int nsplit, float* part, int* ticket, float* out32, int64_t ldo,
-                            __half* outxs, cudaStream_t st, const AttnRope* rope) {
-  Q8_CHECK_ARG(nkv > 0 && nh % nkv == 0 && nh / nkv <= 8, "attention decode: GQA group must be <= 8");
-  Q8_CHECK_ARG(nsplit >= 1 && nsplit <= ATTD_MAXSPLIT && (nsplit == 1 || (part && ticket)),
-               "attention decode: bad split count %d", nsplit);
-  if (T <= 0) return Q8_OK;
-  AttnDecArgs a{q, ldq, pos, seq, T, nh, nkv, kp, vp, page, bt, max_pages, nsplit, part, ticket, out32, ldo, outxs,
-                nullptr, nullptr, nullptr, 0.f, nullptr, nullptr};
-  if (rope) {
-    Q8_CHECK_ARG(rope->inv_freq && rope->kw == kp && rope->vw == vp, "attention decode: bad rope arguments");
-    a.inv_freq = rope->inv_freq;
-    a.qn = rope->qn;
-    a.kn = rope->kn;
-    a.eps = rope->eps;
-    a.kw = rope->kw;
-    a.vw = rope->vw;
-  }
-  dim3 grid(T * nkv, nsplit);
-  const bool g4 = nh / nkv <= 4;
-  const dim3 blk(ATTD_W * 32);
-  if (hd == 128 && g4) return launch_pdl("k_attn_decode", k_attn_decode<128, 4>, grid, blk, 0, st, a);
-  if (hd == 128) return launch_pdl("k_attn_decode", k_attn_decode<128, 8>, grid, blk, 0, st, a);
-  if (hd == 64 && g4) return launch_pdl("k_attn_decode", k_attn_decode<64, 4>, grid, blk, 0, st, a);
-  if (hd == 64) return launch_pdl("k_attn_decode", k_attn_decode<64, 8>, grid, blk, 0, st, a);
-  set_error("attention decode: head_dim %d unsupported", hd);
-  return Q8_ERR_ARG;
-}
-
 // ------------------------------------------------------------------ argmax
 // k_argmax (src/llama_common.mojo:493-519): one CTA per row; lowest index wins
 // ties (numpy.argmax), where the reference's 32-lane tree keeps the lower lane.
@@ -963,9 +642,8 @@ extern "C" int q8op_attention(const float* q, int64_t ldq, int64_t T, const int3
   const int G = n_heads / n_kv;
   const int items = (int)T * n_kv;
   // every token is an independent query (one per item); split the context so
-  // that the grid covers the GPU (at most max_pages*page/64 keys per split)
-  int nsplit = std::max(1, std::min(ceil_div(2 * num_sms(), items), ceil_div((int64_t)max_pages * page, 64)));
-  nsplit = std::min(nsplit, ATTD_MAXSPLIT);
+  // that the grid covers the GPU
+  const int nsplit = attention_decode_nsplit(items, (int)std::min<int64_t>((int64_t)max_pages * page, 1 << 30));
   float* part = nullptr;
   int* ticket = nullptr;
   if (nsplit > 1) {
