@@ -8,6 +8,7 @@
 //   Weights arena, upload_all  src/resident.mojo:15-60
 //   Acts bump arena            src/llama_common.mojo:578-606
 //   SafeTensors                src/safetensors.mojo:17-96
+#include "q8_allreduce.h"
 #include "q8_decode_mk.h"
 #include "q8_kernels.h"
 #include "safetensors.h"
@@ -154,6 +155,8 @@ struct q8_ctx {
   int qb_max = 1;
   cudaStream_t st = nullptr;
   ncclComm_t comm = nullptr;
+  ArState ar;             // one-shot P2P allreduce for decode (TP > 1)
+  int* ar_status_pin = nullptr;
   std::string err;
 
   uint8_t* warena = nullptr;
@@ -259,6 +262,11 @@ static int allreduce(q8_ctx* c, float* buf, size_t n) {
   }
   return Q8_OK;
 }
+
+// Decode-sized row-parallel sums: h += sum over ranks of part on the P2P path
+// (the next RMSNorm then runs in the GEMV prologue); returns false when the
+// batch is too large for it, so the caller keeps NCCL + the RMSNorm kernel.
+static bool p2p_fits(q8_ctx* c, int T) { return c->ar.ok && (int64_t)T * c->H <= c->ar.slot; }
 
 // Runs T tokens whose ids/pos/seq (and query blocks, when qb_tok0 != null) are
 // already in the device buffers.  Produces logits + argmax for token rows
@@ -369,8 +377,12 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
     } else {
       PROF(c, "gemv_o", gemv_bytes(T, c->qd, H),
            gemm_dispatch(EPI_STORE, c->ao32, c->qd, c->xs_ao, T, c->qd, w.o, H, c->ypart, H, nullptr, st));
-      PROF(c, "allreduce", (double)T * H * 4.0, allreduce(c, c->ypart, (size_t)T * H));
-      pending = c->ypart;
+      if (!blocks && p2p_fits(c, T)) {
+        PROF(c, "allreduce", (double)T * H * 4.0 * c->tp_size, ar_launch(c->ar, c->ypart, c->h, T * H, st));
+      } else {
+        PROF(c, "allreduce", (double)T * H * 4.0, allreduce(c, c->ypart, (size_t)T * H));
+        pending = c->ypart;
+      }
     }
     if (tc) {
       PROF(c, "rmsnorm", (double)T * H * (pending ? 14.0 : 10.0),
@@ -404,8 +416,12 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
     } else {
       PROF(c, "gemv_down", gemv_bytes(T, c->F, H),
            gemm_dispatch(EPI_STORE, c->act32, c->F, c->xs_act, T, c->F, w.down, H, c->ypart, H, nullptr, st));
-      PROF(c, "allreduce", (double)T * H * 4.0, allreduce(c, c->ypart, (size_t)T * H));
-      pending = c->ypart;
+      if (!blocks && p2p_fits(c, T)) {
+        PROF(c, "allreduce", (double)T * H * 4.0 * c->tp_size, ar_launch(c->ar, c->ypart, c->h, T * H, st));
+      } else {
+        PROF(c, "allreduce", (double)T * H * 4.0, allreduce(c, c->ypart, (size_t)T * H));
+        pending = c->ypart;
+      }
     }
   }
   if (lrows <= 0) return Q8_OK;
@@ -450,10 +466,19 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
 // with the call's other results, checked after the call's synchronize.
 static int mk_status_copy(q8_ctx* c) {
   if (c->mk) Q8_CUDA(cudaMemcpyAsync(c->mk_status_pin, c->mk_status, 4, cudaMemcpyDeviceToHost, c->st));
+  if (c->ar.ok) Q8_CUDA(cudaMemcpyAsync(c->ar_status_pin, c->ar.status, 4, cudaMemcpyDeviceToHost, c->st));
   return Q8_OK;
 }
 
 static int mk_status_check(q8_ctx* c) {
+  if (c->ar.ok && *c->ar_status_pin != 0) {
+    const int v = *c->ar_status_pin;
+    *c->ar_status_pin = 0;
+    Q8_CUDA(cudaMemsetAsync(c->ar.status, 0, 4, c->st));
+    Q8_CUDA(cudaStreamSynchronize(c->st));
+    set_error("tensor-parallel allreduce: a peer flag wait timed out (device status %d)", v);
+    return Q8_ERR_COMM;
+  }
   if (!c->mk || *c->mk_status_pin == 0) return Q8_OK;
   const int v = *c->mk_status_pin;
   *c->mk_status_pin = 0;
@@ -575,6 +600,8 @@ static int destroy_impl(q8_ctx* c) {
   for (auto& kv : c->g_decode) cudaGraphExecDestroy(kv.second);
   for (auto& kv : c->g_gen) cudaGraphExecDestroy(kv.second);
   for (auto& e : c->ev_pool) { cudaEventDestroy(e.first); cudaEventDestroy(e.second); }
+  ar_teardown(&c->ar);
+  if (c->ar_status_pin) cudaFreeHost(c->ar_status_pin);
   if (c->comm) ncclCommDestroy(c->comm);
   void* ptrs[] = {c->warena, c->kpool, c->vpool, c->bt_d, c->inv_freq_d, c->ids_d, c->pos_d, c->seq_d,
                   c->qb_tok0_d, c->qb_len_d, c->argmax_d, c->hist_d, c->ctr_d, c->ticket_d, c->h, c->qkv, c->ypart,
@@ -858,6 +885,13 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
     memcpy(&id, nccl_id, 128);
     ncclResult_t r = ncclCommInitRank(&c->comm, tp_size, id, tp_rank);
     if (r != ncclSuccess) return bail((set_error("ncclCommInitRank: %s", ncclGetErrorString(r)), Q8_ERR_COMM));
+    // decode-sized row-parallel sums over P2P (every rank takes this step)
+    if ((s = ar_setup(&c->ar, c->comm, tp_size, tp_rank, (int64_t)std::max(1, max_seqs) * H, c->st))) return bail(s);
+    if (c->ar.ok) {
+      if (cudaMallocHost((void**)&c->ar_status_pin, 4) != cudaSuccess)
+        return bail((set_error("pinned status allocation failed"), Q8_ERR_OOM));
+      *c->ar_status_pin = 0;
+    }
   }
   *out = c;
   return Q8_OK;
