@@ -81,6 +81,9 @@ struct AttnArgs {
 };
 int attention_init();
 int attention_launch(const AttnArgs& a, cudaStream_t st);
+// tensor-core prefill attention (q8_attn_tc.cu) for query blocks of 9..64 rows
+bool attention_tc_supported(const AttnArgs& a);
+int attention_tc_launch(const AttnArgs& a, cudaStream_t st);
 size_t attention_part_floats(int nqb, int nkv, int nsplit, int qb_max, int group, int hd);
 
 size_t attention_decode_part_floats(int T, int nkv, int nsplit, int group, int hd);

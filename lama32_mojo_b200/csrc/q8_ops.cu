@@ -431,6 +431,15 @@ int attention_launch(const AttnArgs& a, cudaStream_t st) {
   Q8_CHECK_ARG(a.qb_max * G <= 64, "attention: query block x group must be <= 64");
   Q8_CHECK_ARG(a.nsplit >= 1 && (a.nsplit == 1 || a.part), "attention: split needs scratch");
   if (a.nqb <= 0) return Q8_OK;
+  if (attention_tc_supported(a)) {
+    Q8_TRY(attention_tc_launch(a, st));
+    if (a.nsplit > 1) {
+      if (a.hd == 128) k_attn_combine<128, 64><<<dim3(a.nqb, a.nkv), 128, 0, st>>>(a);
+      else k_attn_combine<64, 64><<<dim3(a.nqb, a.nkv), 128, 0, st>>>(a);
+      Q8_TRY(launch_check("k_attn_combine"));
+    }
+    return Q8_OK;
+  }
   const bool small = a.qb_max * G <= 8;
   switch (a.hd) {
     case 64: return small ? attn_run<64, 8>(a, st) : attn_run<64, 64>(a, st);
