@@ -135,25 +135,37 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) k_attn_tc(AttnArgs a) {
 
   for (int j0 = k_lo; j0 < k_hi; j0 += ATC_TK) {
     __syncthreads();  // the previous tile is consumed (first pass: qpos is visible)
-    for (int i = threadIdx.x; i < ATC_TK * HD / 4; i += ATC_THREADS) {
-      const int jj = i / (HD / 4), d = (i % (HD / 4)) * 4, j = j0 + jj;
-      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-      if (j < k_hi) {
-        const int pg = btr[j / a.page];
-        const int64_t off = (((int64_t)pg * a.nkv + kvh) * a.page + (j % a.page)) * HD + d;
-        kv = *reinterpret_cast<const float4*>(a.kp + off);
-        vv = *reinterpret_cast<const float4*>(a.vp + off);
+    // four rows' loads in flight per thread before any conversion
+    for (int i0 = threadIdx.x; i0 < ATC_TK * HD / 4; i0 += 4 * ATC_THREADS) {
+      float4 kv[4], vv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * ATC_THREADS;
+        const int jj = i / (HD / 4), d = (i % (HD / 4)) * 4, j = j0 + jj;
+        kv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        vv[u] = kv[u];
+        if (j < k_hi) {
+          const int pg = btr[j / a.page];
+          const int64_t off = (((int64_t)pg * a.nkv + kvh) * a.page + (j % a.page)) * HD + d;
+          kv[u] = *reinterpret_cast<const float4*>(a.kp + off);
+          vv[u] = *reinterpret_cast<const float4*>(a.vp + off);
+        }
       }
-      uint32_t h0, l0_, h1, l1_;
-      const int e = atc_swz<HD>(jj, d);
-      atc_split2(kv.x, kv.y, h0, l0_);
-      atc_split2(kv.z, kv.w, h1, l1_);
-      *reinterpret_cast<uint2*>(S.kh + e) = make_uint2(h0, h1);
-      *reinterpret_cast<uint2*>(S.kl + e) = make_uint2(l0_, l1_);
-      atc_split2(vv.x, vv.y, h0, l0_);
-      atc_split2(vv.z, vv.w, h1, l1_);
-      *reinterpret_cast<uint2*>(S.vh + e) = make_uint2(h0, h1);
-      *reinterpret_cast<uint2*>(S.vl + e) = make_uint2(l0_, l1_);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * ATC_THREADS;
+        const int jj = i / (HD / 4), d = (i % (HD / 4)) * 4;
+        uint32_t h0, l0_, h1, l1_;
+        const int e = atc_swz<HD>(jj, d);
+        atc_split2(kv[u].x, kv[u].y, h0, l0_);
+        atc_split2(kv[u].z, kv[u].w, h1, l1_);
+        *reinterpret_cast<uint2*>(S.kh + e) = make_uint2(h0, h1);
+        *reinterpret_cast<uint2*>(S.kl + e) = make_uint2(l0_, l1_);
+        atc_split2(vv[u].x, vv[u].y, h0, l0_);
+        atc_split2(vv[u].z, vv[u].w, h1, l1_);
+        *reinterpret_cast<uint2*>(S.vh + e) = make_uint2(h0, h1);
+        *reinterpret_cast<uint2*>(S.vl + e) = make_uint2(l0_, l1_);
+      }
     }
     __syncthreads();
 
@@ -163,20 +175,21 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) k_attn_tc(AttnArgs a) {
     for (int n = 0; n < NT; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < KS; ++kk) {
+      uint32_t bh[NT / 2][4], bl[NT / 2][4];
 #pragma unroll
       for (int np = 0; np < NT; np += 2) {
         // matrices: (keys 8np.., dims 16kk..), (8np.., 16kk+8..), (8np+8.., 16kk..), (8np+8.., 16kk+8..)
         const int key = 8 * np + ((mi >> 1) << 3) + rr, dim = 16 * kk + ((mi & 1) << 3);
-        uint32_t bh[4], bl[4];
-        atc_ldsm_x4(bh, S.kh + atc_swz<HD>(key, dim));
-        atc_ldsm_x4(bl, S.kl + atc_swz<HD>(key, dim));
-        atc_mma(s[np], qh[kk], bh[0], bh[1]);
-        atc_mma(s[np], qh[kk], bl[0], bl[1]);
-        atc_mma(s[np], ql[kk], bh[0], bh[1]);
-        atc_mma(s[np + 1], qh[kk], bh[2], bh[3]);
-        atc_mma(s[np + 1], qh[kk], bl[2], bl[3]);
-        atc_mma(s[np + 1], ql[kk], bh[2], bh[3]);
+        atc_ldsm_x4(bh[np / 2], S.kh + atc_swz<HD>(key, dim));
+        atc_ldsm_x4(bl[np / 2], S.kl + atc_swz<HD>(key, dim));
       }
+      // one split term across all n-tiles before the next: independent MMAs back to back
+#pragma unroll
+      for (int n = 0; n < NT; ++n) atc_mma(s[n], qh[kk], bh[n / 2][(n & 1) * 2], bh[n / 2][(n & 1) * 2 + 1]);
+#pragma unroll
+      for (int n = 0; n < NT; ++n) atc_mma(s[n], qh[kk], bl[n / 2][(n & 1) * 2], bl[n / 2][(n & 1) * 2 + 1]);
+#pragma unroll
+      for (int n = 0; n < NT; ++n) atc_mma(s[n], ql[kk], bh[n / 2][(n & 1) * 2], bh[n / 2][(n & 1) * 2 + 1]);
     }
 
     // causal mask, online softmax (rows r0: c0/c1, r1: c2/c3)
@@ -232,18 +245,21 @@ __global__ void __launch_bounds__(ATC_THREADS, 2) k_attn_tc(AttnArgs a) {
       atc_split2(s[2 * kk + 1][0], s[2 * kk + 1][1], ph[2], pl[2]);
       atc_split2(s[2 * kk + 1][2], s[2 * kk + 1][3], ph[3], pl[3]);
 #pragma unroll
-      for (int np = 0; np < ON; np += 2) {
+      for (int np = 0; np < ON; np += 4) {
         // matrices (transposed): (keys 16kk.., dims 8np..), (16kk+8.., 8np..), (16kk.., 8np+8..), (16kk+8.., 8np+8..)
-        const int key = 16 * kk + ((mi & 1) << 3) + rr, dim = 8 * np + ((mi >> 1) << 3);
-        uint32_t vh[4], vl[4];
-        atc_ldsm_x4_t(vh, S.vh + atc_swz<HD>(key, dim));
-        atc_ldsm_x4_t(vl, S.vl + atc_swz<HD>(key, dim));
-        atc_mma(o[np], ph, vh[0], vh[1]);
-        atc_mma(o[np], ph, vl[0], vl[1]);
-        atc_mma(o[np], pl, vh[0], vh[1]);
-        atc_mma(o[np + 1], ph, vh[2], vh[3]);
-        atc_mma(o[np + 1], ph, vl[2], vl[3]);
-        atc_mma(o[np + 1], pl, vh[2], vh[3]);
+        uint32_t vh[2][4], vl[2][4];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int key = 16 * kk + ((mi & 1) << 3) + rr, dim = 8 * (np + 2 * h) + ((mi >> 1) << 3);
+          atc_ldsm_x4_t(vh[h], S.vh + atc_swz<HD>(key, dim));
+          atc_ldsm_x4_t(vl[h], S.vl + atc_swz<HD>(key, dim));
+        }
+#pragma unroll
+        for (int n = 0; n < 4; ++n) atc_mma(o[np + n], ph, vh[n / 2][(n & 1) * 2], vh[n / 2][(n & 1) * 2 + 1]);
+#pragma unroll
+        for (int n = 0; n < 4; ++n) atc_mma(o[np + n], ph, vl[n / 2][(n & 1) * 2], vl[n / 2][(n & 1) * 2 + 1]);
+#pragma unroll
+        for (int n = 0; n < 4; ++n) atc_mma(o[np + n], pl, vh[n / 2][(n & 1) * 2], vh[n / 2][(n & 1) * 2 + 1]);
       }
     }
   }
