@@ -63,6 +63,8 @@ struct AdArgs {
   int* ticket;      // [T*nkv], zero at rest
   float* out32; int64_t ldo;
   __half* outxs;
+  __half* out16;           // optional f16 rows [T][nh*hd] (tensor-core GEMM input)
+  int64_t out16lo;         // > 0: f16 remainders at out16 + out16lo
   const float* inv_freq;   // RoPE + QK-norm + KV append fused when set
   const uint16_t* qn;
   const uint16_t* kn;
@@ -126,6 +128,12 @@ __device__ __forceinline__ void ad_write_out(const AdArgs& a, int K, int tok, in
     split_f16(v, hi, lo);
     a.outxs[xs_index(tok, col, K, 0)] = hi;
     a.outxs[xs_index(tok, col, K, 1)] = lo;
+  }
+  if (a.out16) {
+    const int64_t i = (int64_t)tok * K + col;
+    const __half hv = __float2half_rn(v);
+    a.out16[i] = hv;
+    if (a.out16lo) a.out16[a.out16lo + i] = __float2half_rn(v - __half2float(hv));
   }
 }
 
@@ -546,7 +554,8 @@ size_t attention_decode_part_floats(int T, int nkv, int nsplit, int group, int h
 int attention_decode_launch(const float* q, int64_t ldq, int T, const int32_t* pos, const int32_t* seq, int nh,
                             int nkv, int hd, const float* kp, const float* vp, int page, const int32_t* bt,
                             int max_pages, int nsplit, float* part, int* ticket, float* out32, int64_t ldo,
-                            __half* outxs, cudaStream_t st, const AttnRope* rope, int64_t pool_rows) {
+                            __half* outxs, cudaStream_t st, const AttnRope* rope, int64_t pool_rows,
+                            __half* out16, int64_t out16lo) {
   Q8_CHECK_ARG(nkv > 0 && nh % nkv == 0 && nh / nkv <= 8, "attention decode: GQA group must be <= 8");
   Q8_CHECK_ARG(nsplit >= 1 && nsplit <= AD_MAXSPLIT && (nsplit == 1 || (part && ticket)),
                "attention decode: bad split count %d", nsplit);
@@ -554,7 +563,7 @@ int attention_decode_launch(const float* q, int64_t ldq, int T, const int32_t* p
   Q8_CHECK_ARG(((uintptr_t)kp & 15) == 0 && ((uintptr_t)vp & 15) == 0, "attention decode: pools must be 16-byte aligned");
   if (T <= 0) return Q8_OK;
   AdArgs a{q, ldq, pos, seq, T, nh, nkv, kp, vp, page, bt, max_pages, part, ticket, out32, ldo, outxs,
-           nullptr, nullptr, nullptr, 0.f, nullptr, nullptr};
+           out16, out16lo, nullptr, nullptr, nullptr, 0.f, nullptr, nullptr};
   if (rope) {
     Q8_CHECK_ARG(rope->inv_freq && rope->kw == kp && rope->vw == vp, "attention decode: bad rope arguments");
     a.inv_freq = rope->inv_freq;

@@ -553,6 +553,14 @@ int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int64_t x16lo, int 
   return launch_check("k_gemm_q8_tc");
 }
 
+int tc_min_tokens() {
+  static const int v = [] {
+    const char* e = getenv("Q8_TC_MIN");
+    return e ? std::max(1, atoi(e)) : kTcMinTokens;
+  }();
+  return v;
+}
+
 int gemm_tc_poll_error() {
   int v = 0;
   Q8_CUDA(cudaMemcpyFromSymbol(&v, g_q8_device_error, sizeof(int)));

@@ -848,7 +848,7 @@ static int op_gemm_common(int epi, const void* x, int x_dtype, int64_t ldx, int6
   Q8_CHECK_ARG(M < (1 << 30) && K < (1 << 30) && N < (1 << 30), "q8op_gemm: dims too large");
   cudaStream_t st = (cudaStream_t)stream;
   void* xs = nullptr;
-  if (M >= kTcMinTokens && K % 512 == 0 && ((uintptr_t)w & 15) == 0) {
+  if (M >= tc_min_tokens() && K % 512 == 0 && ((uintptr_t)w & 15) == 0) {
     // prefill-sized batch: f16 rows (split hi + lo unless fast mode) ->
     // tensor-core GEMM
     const int64_t lo = gemm_tc_exact() ? M * K : 0;

@@ -45,6 +45,8 @@ int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int64_t x16lo, int 
 int gemm_tc_poll_error();
 // Smallest token batch the model runtime sends to the tensor-core GEMM.
 constexpr int kTcMinTokens = 128;
+// token count from which batches use the tensor-core GEMM (Q8_TC_MIN, default kTcMinTokens)
+int tc_min_tokens();
 // x (Q8_F32 / Q8_BF16 / Q8_F16 rows) -> plain f16 rows [M][K].
 int to_f16_launch(const void* x, int dtype, int64_t ldx, int M, int K, __half* y, cudaStream_t st,
                   int64_t ylo = 0);
@@ -104,7 +106,8 @@ int attention_decode_launch(const float* q, int64_t ldq, int T, const int32_t* p
                             int nkv, int hd, const float* kp, const float* vp, int page, const int32_t* bt,
                             int max_pages, int nsplit, float* part, int* ticket, float* out32, int64_t ldo,
                             __half* outxs, cudaStream_t st, const AttnRope* rope = nullptr,
-                            int64_t pool_rows = 0);  // rows of each pool (0: unknown)
+                            int64_t pool_rows = 0,  // rows of each pool (0: unknown)
+                            __half* out16 = nullptr, int64_t out16lo = 0);
 
 int argmax_prepare();  // per-device scratch of the wide-row argmax (outside capture)
 int argmax_launch(const float* logits, int64_t rows, int64_t n, int64_t ld, int32_t* out,

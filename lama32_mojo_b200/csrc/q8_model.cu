@@ -155,6 +155,7 @@ struct q8_ctx {
   int qb_max = 1;
   cudaStream_t st = nullptr;
   ncclComm_t comm = nullptr;
+  int tc_dmin = 32;        // decode batches from this size run the tensor-core pipeline
   ArState ar;             // one-shot P2P allreduce for decode (TP > 1)
   int* ar_status_pin = nullptr;
   std::string err;
@@ -306,9 +307,10 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
   // small token batches fuse RMSNorm into the GEMV prologue (K = hidden fits
   // the shared-memory staging); large batches keep the standalone kernel
   const bool fuse_norm = H <= 6144 && T <= 64;
-  // prefill-sized batches run the tensor-core GEMM on f16 activation rows;
-  // the XS buffers double as those rows (they hold twice the elements)
-  const bool tc = c->tc && blocks && T >= kTcMinTokens;
+  // prefill-sized batches, and decode batches of at least c->tc_dmin
+  // sequences, run the tensor-core GEMM on f16 activation rows; the XS
+  // buffers double as those rows (they hold twice the elements)
+  const bool tc = c->tc && T >= (blocks ? kTcMinTokens : c->tc_dmin);
   __half* xn16 = c->xs_in;
   __half* ao16 = c->xs_ao;
   __half* act16 = c->xs_act;
@@ -360,8 +362,9 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
                           const_cast<float*>(a.vp)};
       PROF(c, "attention", kv_bytes_hint / c->cfg.layers + (double)T * c->qd * 8.0,
            attention_decode_launch(c->qkv, nqkv, T, c->pos_d, c->seq_d, c->nh, c->nkv, c->hd, a.kp, a.vp, c->page,
-                                   c->bt_d, c->max_pages, nsplit, c->part, c->ticket_d, c->ao32, c->qd,
-                                   c->xs_ao, st, &rope, (int64_t)(c->layer_kv / c->hd)));
+                                   c->bt_d, c->max_pages, nsplit, c->part, c->ticket_d, tc ? nullptr : c->ao32,
+                                   c->qd, tc ? nullptr : c->xs_ao, st, &rope, (int64_t)(c->layer_kv / c->hd),
+                                   tc ? ao16 : nullptr, tc ? loQ : 0));
     }
     if (tc) {
       PROF(c, "gemm_o", gemv_bytes(T, c->qd, H),
@@ -427,7 +430,13 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
   if (lrows <= 0) return Q8_OK;
   float* hrow = c->h + (size_t)lrow0 * H;
   const float* prow = pending ? pending + (size_t)lrow0 * H : nullptr;
-  if (!prow && fuse_norm) {
+  if (tc && lrows >= c->tc_dmin) {
+    PROF(c, "rmsnorm", (double)lrows * H * 10.0,
+         rmsnorm_launch(hrow, prow, c->final_norm, lrows, H, c->cfg.eps, nullptr, nullptr, xn16, st, loH));
+    PROF(c, "gemv_lmhead", gemv_bytes(lrows, H, c->V_loc),
+         gemm_tc_launch(EPI_STORE, xn16, H, loH, lrows, H, c->lm_head, c->V_loc, c->logits, c->V_loc, nullptr, 0, 0,
+                        st));
+  } else if (!prow && fuse_norm) {
     PROF(c, "gemv_lmhead", gemv_bytes(lrows, H, c->V_loc),
          gemv_rms_launch(EPI_STORE, hrow, H, c->final_norm, c->cfg.eps, lrows, H, c->lm_head, c->V_loc, c->logits,
                          c->V_loc, nullptr, st));
@@ -684,6 +693,10 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
     // Q8_TC=0 keeps prefill on the GEMV kernels (A/B comparisons)
     const char* e = getenv("Q8_TC");
     c->tc = C.hidden % 512 == 0 && c->qd % 512 == 0 && c->F % 512 == 0 && !(e && e[0] == '0');
+    // Q8_TC_DECODE_MIN: decode batches from this many sequences use the
+    // tensor-core pipeline (default 32; the GEMV kernels below it)
+    const char* d = getenv("Q8_TC_DECODE_MIN");
+    c->tc_dmin = d ? std::max(1, atoi(d)) : 32;
   }
   c->V = C.vocab;
   c->V_loc = C.vocab / tp_size;
@@ -1375,6 +1388,7 @@ static int decode_impl(q8_ctx* c, const int32_t* ids, const int32_t* seqs, int B
   Q8_TRY(mk_status_copy(c));
   Q8_CUDA(cudaStreamSynchronize(c->st));
   Q8_TRY(mk_status_check(c));
+  if (c->tc && B >= c->tc_dmin) Q8_TRY(gemm_tc_poll_error());
   for (int b = 0; b < B; ++b) c->n_cached[seqs[b]] += 1;
   return Q8_OK;
 }
@@ -1407,6 +1421,7 @@ static int generate_impl(q8_ctx* c, const int32_t* first, const int32_t* seqs, i
   Q8_TRY(mk_status_copy(c));
   Q8_CUDA(cudaStreamSynchronize(c->st));
   Q8_TRY(mk_status_check(c));
+  if (c->tc && B >= c->tc_dmin) Q8_TRY(gemm_tc_poll_error());
   for (int b = 0; b < B; ++b) c->n_cached[seqs[b]] += steps;
   return Q8_OK;
 }

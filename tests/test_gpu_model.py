@@ -120,7 +120,13 @@ def test_incremental_and_chunked_match_oracle(cuda, cfgname):
     assert got == toks
 
 
-def test_batched_decode_and_generate(cuda):
+@pytest.mark.parametrize("tc_min", [None, "2"])
+def test_batched_decode_and_generate(cuda, tc_min, monkeypatch):
+    """B=4 host-driven and on-device decode against the oracle; with
+    Q8_TC_DECODE_MIN=2 the batch runs the tensor-core layer pipeline (f16
+    hi/lo activation rows, decode attention writing them, tcgen05 GEMMs)."""
+    if tc_min:
+        monkeypatch.setenv("Q8_TC_DECODE_MIN", tc_min)
     cfgname = "tiny-llama-untied"
     ocfg = O.PRESETS[cfgname]
     m = build(cfgname, maxlen=64, max_seqs=4)
@@ -267,6 +273,29 @@ def test_tc_prefill_vs_oracle(cuda):
     for L in (0, 2):
         close(m2.forward_hidden(ids[:200], L), o2.trace[f"after_layer{L}"])
     m2.close()
+
+
+@pytest.mark.parametrize("cfgname", ["tiny-llama", "tiny-qwen3"])
+def test_prefill_attention_context_splits(cuda, cfgname):
+    """Prompt chunks of 64 after a growing prefix: the third and fourth chunks
+    attend to more than 128 positions, so the tensor-core prefill attention
+    splits the context (partials + combine) for head_dim 64 (tiny-llama) and
+    128 (tiny-qwen3); logits and greedy tokens against the oracle."""
+    ocfg = O.PRESETS[cfgname]
+    ck = O.make_q8_checkpoint(ocfg)
+    orc = O.OracleModel(ocfg, ck)
+    ids = O.random_ids(ocfg, 230, seed=21)
+    ref = orc.forward(ids)
+    toks = [int(np.argmax(ref))]
+    for _ in range(3):
+        toks.append(orc.forward_argmax([toks[-1]]))
+    m = build(cfgname, maxlen=256, max_tokens=64)
+    close(m.forward(ids), ref)
+    got = [int(np.argmax(ref))]
+    for _ in range(3):
+        got.append(m.forward_argmax([got[-1]]))
+    assert got == toks
+    m.close()
 
 
 @pytest.mark.parametrize("cfgname", ["tiny-llama", "tiny-qwen3", "tiny-llama-untied"])
