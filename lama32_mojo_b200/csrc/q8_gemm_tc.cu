@@ -49,7 +49,21 @@ struct TcParams {
   __half* y16;       // SwiGLU only: f16 copy of the output [M][ld16]
   int64_t ld16;
   int64_t y16lo;     // > 0: also the f16 remainder a - f16(a), at y16 + y16lo
+  int ksplit;        // K split across gridDim.z CTAs (1: none)
+  float* ws;         // split partials [tile][ksplit][TC_BM][BN]
+  int* tickets;      // [tile], zero at rest
 };
+
+// split-K semaphore: release this CTA's partial stores (made visible to the
+// calling thread by a barrier), acquire the other CTAs'
+__device__ __forceinline__ int tc_ticket_add(int* t) {
+  int old;
+  asm volatile("fence.acq_rel.gpu;\n\tatom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(t) : "memory");
+  return old;
+}
+
+// barrier 3 over the 8 converter / epilogue warps
+__device__ __forceinline__ void epi_bar_all() { asm volatile("bar.sync 3, 256;" ::: "memory"); }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
@@ -191,7 +205,11 @@ __global__ void __launch_bounds__(320, 1) k_gemm_q8_tc(const __grid_constant__ C
   const int r0 = blockIdx.y * (EPI == EPI_SWIGLU ? TC_BM / 2 : TC_BM);  // first output row (pair)
   // weight rows of the two 64-row code boxes
   const int rowA = r0, rowB = (EPI == EPI_SWIGLU) ? p.N + r0 : r0 + 64;
-  const int nk = p.K / TC_BK;  // a multiple of 8
+  // K range of this CTA: whole blocks of 8 k-tiles (one uint4 of group scales)
+  const int nkb = p.K / (8 * TC_BK);
+  const int kb0 = (int)(((int64_t)blockIdx.z * nkb) / gridDim.z), kb1 = (int)(((int64_t)(blockIdx.z + 1) * nkb) / gridDim.z);
+  const int kt0 = 8 * kb0, nk = 8 * (kb1 - kb0);  // k-tiles [kt0, kt0 + nk)
+  __shared__ int s_last;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -216,9 +234,9 @@ __global__ void __launch_bounds__(320, 1) k_gemm_q8_tc(const __grid_constant__ C
   if (warp == 0) {
     // ---------------- TMA producer
     if (lane == 0) {
-      for (int kt = 0; kt < nk; ++kt) {
-        const int s = kt % S;
-        const uint32_t ph = (kt / S) & 1;
+      for (int lk = 0; lk < nk; ++lk) {
+        const int kt = kt0 + lk, s = lk % S;
+        const uint32_t ph = (lk / S) & 1;
         mbar_wait(&empty[s], ph ^ 1);
         uint8_t* st = smem + s * Cfg::STAGE;
         mbar_arrive_expect_tx(&full[s], TC_CODES + Cfg::B);
@@ -234,9 +252,9 @@ __global__ void __launch_bounds__(320, 1) k_gemm_q8_tc(const __grid_constant__ C
     // N = BN (bits 17-22: N >> 3), M = 128 (bits 24-28: M >> 4)
     const uint32_t idesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
     if (lane == 0) {
-      for (int kt = 0; kt < nk; ++kt) {
-        const int s = kt % S;
-        const uint32_t ph = (kt / S) & 1;
+      for (int lk = 0; lk < nk; ++lk) {
+        const int s = lk % S;
+        const uint32_t ph = (lk / S) & 1;
         mbar_wait(&full[s], ph);
         mbar_wait(&conv[s], ph);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -244,7 +262,7 @@ __global__ void __launch_bounds__(320, 1) k_gemm_q8_tc(const __grid_constant__ C
         const uint64_t da = sw128_desc(st), db = sw128_desc(st + Cfg::A);
 #pragma unroll
         for (int k = 0; k < TC_BK / 16; ++k) {  // K = 16 -> 32 B further inside the swizzle atom
-          tc_mma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (kt | k) != 0);
+          tc_mma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (lk | k) != 0);
           if constexpr (X) {
             // hi x lo and lo x hi; lo x lo is below the f32 accumulation error
             const uint64_t dal = sw128_desc(st + TC_A), dbl = sw128_desc(st + Cfg::A + Cfg::B1);
@@ -280,20 +298,20 @@ __global__ void __launch_bounds__(320, 1) k_gemm_q8_tc(const __grid_constant__ C
     const uint4 zero4 = make_uint4(0, 0, 0, 0);
     uint4 snext[4];
 #pragma unroll
-    for (int it = 0; it < 4; ++it) snext[it] = srow[it] ? __ldg(srow[it]) : zero4;
-    for (int kb = 0; kb < nk / 8; ++kb) {
+    for (int it = 0; it < 4; ++it) snext[it] = srow[it] ? __ldg(srow[it] + kb0) : zero4;
+    for (int kb = kb0; kb < kb1; ++kb) {
       // scales of k-tiles 8kb..8kb+7 (one uint4 per row); fetch the next block
       uint4 sblk[4];
 #pragma unroll
       for (int it = 0; it < 4; ++it) {
         sblk[it] = snext[it];
-        snext[it] = (srow[it] && kb + 1 < nk / 8) ? __ldg(srow[it] + kb + 1) : zero4;
+        snext[it] = (srow[it] && kb + 1 < kb1) ? __ldg(srow[it] + kb + 1) : zero4;
       }
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) {
-        const int kt = 8 * kb + 2 * jj + grp;
-        const int s = kt % S;
-        const uint32_t ph = (kt / S) & 1;
+        const int lk = 8 * (kb - kb0) + 2 * jj + grp;
+        const int s = lk % S;
+        const uint32_t ph = (lk / S) & 1;
         __half sc[4];
 #pragma unroll
         for (int it = 0; it < 4; ++it) sc[it] = pick_scale(sblk[it], jj, grp);
@@ -334,6 +352,49 @@ __global__ void __launch_bounds__(320, 1) k_gemm_q8_tc(const __grid_constant__ C
     const int q = warp & 3;
     const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16);
     const int cbeg = grp * (BN / 2), cend = cbeg + BN / 2;
+    // split K: every CTA parks its f32 tile; the last CTA of the tile (ticket)
+    // sums the parked tiles in split order and runs the epilogue below
+    const int tile = blockIdx.x + gridDim.x * blockIdx.y;
+    const int arow = 32 * q + lane;  // accumulator row = TMEM lane
+    float* wst = p.ksplit > 1 ? p.ws + (int64_t)tile * p.ksplit * TC_BM * BN : nullptr;
+    bool run_epi = true;
+    if (p.ksplit > 1) {
+#pragma unroll 1
+      for (int c0 = cbeg; c0 < cend; c0 += 32) {
+        float v[32];
+        tmem_ld32(tq + (uint32_t)c0, v);
+        float4* dst = reinterpret_cast<float4*>(wst + ((int64_t)blockIdx.z * TC_BM + arow) * BN + c0);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      }
+      epi_bar_all();
+      if (threadIdx.x == 64) s_last = tc_ticket_add(&p.tickets[tile]) == p.ksplit - 1;
+      epi_bar_all();
+      run_epi = s_last != 0;
+      if (run_epi && threadIdx.x == 64) p.tickets[tile] = 0;  // ready for the next launch
+    }
+    // accumulator columns c0..c0+31 of this thread's row: TMEM, or the sum of
+    // the parked split tiles in split order
+    auto fetch = [&](int c0, float (&v)[32]) {
+      if (p.ksplit <= 1) {
+        tmem_ld32(tq + (uint32_t)c0, v);
+        return;
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = 0.f;
+      for (int z = 0; z < p.ksplit; ++z) {
+        const float4* src = reinterpret_cast<const float4*>(wst + ((int64_t)z * TC_BM + arow) * BN + c0);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 t = __ldcg(src + j);
+          v[4 * j] += t.x;
+          v[4 * j + 1] += t.y;
+          v[4 * j + 2] += t.z;
+          v[4 * j + 3] += t.w;
+        }
+      }
+    };
+    if (run_epi) {
     if constexpr (EPI == EPI_SWIGLU) {
       // every MMA has completed: stage memory is free for the hand-off
       float* xch = reinterpret_cast<float*>(smem) + grp * (64 * 33);  // [64 rows][33] per group
@@ -341,7 +402,7 @@ __global__ void __launch_bounds__(320, 1) k_gemm_q8_tc(const __grid_constant__ C
 #pragma unroll 1
       for (int c0 = cbeg; c0 < cend; c0 += 32) {
         float v[32];
-        tmem_ld32(tq + (uint32_t)c0, v);
+        fetch(c0, v);
         if (q >= 2) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) xch[(32 * (q - 2) + lane) * 33 + j] = v[j];
@@ -369,7 +430,7 @@ __global__ void __launch_bounds__(320, 1) k_gemm_q8_tc(const __grid_constant__ C
 #pragma unroll 1
       for (int c0 = cbeg; c0 < cend; c0 += 32) {
         float v[32];
-        tmem_ld32(tq + (uint32_t)c0, v);
+        fetch(c0, v);
         if (n < p.N) {
           float* col = p.y + (int64_t)(m0 + c0) * p.ldy + n;
           const int mcnt = min(32, p.M - (m0 + c0));
@@ -390,6 +451,7 @@ __global__ void __launch_bounds__(320, 1) k_gemm_q8_tc(const __grid_constant__ C
         }
       }
     }
+    }  // run_epi
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -460,6 +522,11 @@ static int tc_attr_all() {
   return Q8_OK;
 }
 
+// split-K workspace per device: up to TC_WS_TILES parked 128 x 128 f32 tiles
+constexpr int TC_WS_TILES = 320;
+static float* g_tc_ws[64];
+static int* g_tc_tickets[64];
+
 static int tc_init() {
   static bool done[64] = {false};
   static std::mutex mu;
@@ -469,6 +536,13 @@ static int tc_init() {
   if (done[dev & 63]) return Q8_OK;
   Q8_TRY(tc_attr_all<false>());
   Q8_TRY(tc_attr_all<true>());
+  if (cudaMalloc(&g_tc_ws[dev & 63], (size_t)TC_WS_TILES * TC_BM * 128 * 4) != cudaSuccess ||
+      cudaMalloc(&g_tc_tickets[dev & 63], (size_t)TC_WS_TILES * 4) != cudaSuccess ||
+      cudaMemset(g_tc_tickets[dev & 63], 0, (size_t)TC_WS_TILES * 4) != cudaSuccess) {
+    cudaGetLastError();
+    set_error("gemm_tc: split-K workspace allocation failed");
+    return Q8_ERR_OOM;
+  }
   done[dev & 63] = true;
   return Q8_OK;
 }
@@ -544,8 +618,24 @@ int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int64_t x16lo, int 
   }
   Q8_TRY(tc_x_map(enc, &tmx, x16, ld16, M, K, bn));
   Q8_TRY(tc_x_map(enc, &tmxl, X ? x16 + x16lo : x16, ld16, M, K, bn));
-  TcParams p{(const uint8_t*)W, rb, K, N, M, y, ldy, y16, ldy16, y16lo};
+  TcParams p{(const uint8_t*)W, rb, K, N, M, y, ldy, y16, ldy16, y16lo, 1, nullptr, nullptr};
   dim3 grid(ceil_div(M, bn), epi == EPI_SWIGLU ? ceil_div(N, TC_BM / 2) : ceil_div(N, TC_BM));
+  // small batches leave SMs idle: split K (whole 8-tile scale blocks) until
+  // the tiles cover the SMs; the last CTA of a tile sums the parts in order
+  {
+    const int ntile = (int)(grid.x * grid.y), nkb = K / (8 * TC_BK);
+    int ks = 1;
+    if (bn == 128 && ntile < num_sms()) ks = std::min(nkb, std::max(1, num_sms() / ntile));
+    while (ks > 1 && ntile * ks > TC_WS_TILES) --ks;
+    if (ks > 1) {
+      int dev = 0;
+      Q8_CUDA(cudaGetDevice(&dev));
+      p.ksplit = ks;
+      p.ws = g_tc_ws[dev & 63];
+      p.tickets = g_tc_tickets[dev & 63];
+      grid.z = ks;
+    }
+  }
   if (X && bn == 256) tc_launch<256, true>(epi, grid, tmc, tmx, tmxl, p, st);
   else if (X) tc_launch<128, true>(epi, grid, tmc, tmx, tmxl, p, st);
   else if (bn == 256) tc_launch<256, false>(epi, grid, tmc, tmx, tmxl, p, st);
