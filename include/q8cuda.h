@@ -169,6 +169,20 @@ int q8op_attention(const float* q, int64_t ldq, int64_t T, const int32_t* pos,
 int q8op_argmax(const float* logits, int64_t rows, int64_t n, int64_t ld, int32_t* out,
                 void* stream);
 
+/* Temperature + nucleus (top-p) sampling per row — sample()
+ * (src/sample.mojo:15-59) on the device, with the reference's arithmetic
+ * order: candidates are the logits >= max - 16, p = exp((l - max) / temp),
+ * total summed in index order, the nucleus taken largest p first (equal p in
+ * the order of the reference's swap-remove list) while the running sum is
+ * below total * top_p, then the first nucleus entry whose running sum reaches
+ * u * sum.  logits [rows, ld] f32 with n used columns; u [rows] f32 uniform
+ * draws in [0, 1), device memory (the reference draws random_float64(),
+ * src/sample.mojo:55); out [rows] int32.  temp <= 0 is greedy (first
+ * maximum; u may then be NULL).  top_p must be > 0 when temp > 0.  Uses the
+ * per-device op scratch (28 bytes per logit).  exp() is CUDA's expf. */
+int q8op_sample(const float* logits, int64_t rows, int64_t n, int64_t ld, float temp, float top_p,
+                const float* u, int32_t* out, void* stream);
+
 /* ================================================================ model level */
 
 /* Create a context on `device`.  Mirrors QwenQ8/Llama.__init__ + Acts/Weights

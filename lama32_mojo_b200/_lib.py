@@ -63,6 +63,7 @@ SIGNATURES = {
                             _P, _I32, _P],
     "q8op_attention": [_P, _I64, _I64, _P, _P, _I32, _I32, _I32, _P, _P, _I32, _P, _I32, _P, _I64, _P],
     "q8op_argmax": [_P, _I64, _I64, _I64, _P, _P],
+    "q8op_sample": [_P, _I64, _I64, _I64, _F, _F, _P, _P, _P],
     "q8_create": [C.POINTER(q8_config), _I32, _I32, _I32, _I32, _I32, _I32, _P, C.POINTER(_P)],
     "q8_destroy": [_P],
     "q8_nccl_unique_id": [_P],

@@ -112,5 +112,10 @@ int attention_decode_launch(const float* q, int64_t ldq, int T, const int32_t* p
 int argmax_prepare();  // per-device scratch of the wide-row argmax (outside capture)
 int argmax_launch(const float* logits, int64_t rows, int64_t n, int64_t ld, int32_t* out,
                   cudaStream_t st);
+// Temperature + nucleus sampling of rows of logits (q8_sample.cu); u [rows]
+// uniform draws on the device; scratch of sample_scratch_bytes(rows, n).
+size_t sample_scratch_bytes(int rows, int n);
+int sample_launch(const float* logits, int rows, int n, int64_t ld, float temp, float top_p, const float* u,
+                  int32_t* out, void* scratch, size_t scratch_bytes, cudaStream_t st);
 
 }  // namespace q8

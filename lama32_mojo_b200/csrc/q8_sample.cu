@@ -1,0 +1,399 @@
+// Temperature + nucleus (top-p) sampling on the device: sample()
+// (src/sample.mojo:15-59), with the uniform draw supplied per row.
+//
+// The reference, per logits row:
+//   temp <= 0: greedy argmax (first maximum);
+//   candidates: logits >= max - 16 in index order, p = exp((l - max) / temp),
+//   total = their f32 sum in index order; no candidate: argmax;
+//   nucleus: while cum < total * top_p, pick the largest remaining p (the
+//   first one in list order), append it, move the list's last entry into its
+//   place (swap-remove);
+//   r = u * cum; the first nucleus entry whose running sum reaches r.
+// Every f32 sum above is sequential, so the result depends on the order of
+// the additions; this file keeps each order and each rounding:
+//   k_sample_prep   one CTA per row: max / first argmax, candidates compacted
+//                   in index order (per-thread contiguous ranges + a block
+//                   scan), p, and total summed in index order by one warp
+//                   (256 values per round, the next round's loads in flight);
+//   sort            candidates by p, descending (CUB segmented radix sort,
+//                   one segment per row);
+//   k_sample_walk   one warp per row: the running sums of the sorted p (the
+//                   reference's cum after each pick, and also its second
+//                   loop's acc: the same additions in the same order); the
+//                   nucleus ends at the first sum >= target, r = u * cum, and
+//                   the pick is the first sum >= r (binary searches: the sums
+//                   never decrease, p >= 0).
+//   k_sample_ties   only when the chosen entry's p is shared by other
+//                   candidates: which of them the reference picks at that
+//                   point depends on their list positions after every earlier
+//                   swap-remove, so one thread replays the list up to the
+//                   chosen entry, O(1) per removal (rare: equal p needs equal
+//                   or nearly equal logits).
+// Values of exp() come from CUDA's expf; the reference uses Mojo's exp.
+#include "q8_kernels.h"
+
+#include <cub/device/device_segmented_radix_sort.cuh>
+
+#include <float.h>
+#include <math.h>
+
+namespace q8 {
+
+constexpr int SP_THREADS = 1024;
+
+struct SampleWs {
+  int* cidx;      // [R][n] candidate -> token index, index order
+  float* key_in;  // [R][n] candidate p, index order; then the running sums
+  int* val_in;    // [R][n] candidate number; then the replay's candidate -> list position
+  float* key_out; // [R][n] p, descending
+  int* val_out;   // [R][n] candidate number, in key_out's order
+  int* beg;       // [R] segment offsets for the sort
+  int* end;       // [R]
+  int* cnt;       // [R] candidates (0: out already written)
+  float* target;  // [R]
+  int* tie;       // [R] -1, or the nucleus entry whose equal-p group needs the replay
+  int* aux;       // [R][2n] replay: group tags per candidate, then a bitmap of list positions
+};
+
+// 256 consecutive values b0.. of a[0, C) for a warp: lane l holds b0 + 32 k + l
+// (0 past C: adding +0 leaves a sum of non-negative values unchanged)
+__device__ __forceinline__ void sp_ld8(float (&v)[8], const float* a, int b0, int C) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int e = b0 + 32 * k + lane;
+    v[k] = e < C ? a[e] : 0.f;
+  }
+}
+
+__device__ __forceinline__ void sp_merge(float& bv, int& bi, float ov, int oi) {
+  if (ov > bv || (ov == bv && oi < bi)) {
+    bv = ov;
+    bi = oi;
+  }
+}
+
+// exclusive prefix sum of v over the CTA (SP_THREADS threads); *total = sum
+__device__ __forceinline__ int sp_block_scan(int v, int* total) {
+  __shared__ int s_w[SP_THREADS / 32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_w[w] = x;
+  __syncthreads();
+  if (w == 0) {
+    int t = s_w[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += y;
+    }
+    s_w[lane] = t;
+  }
+  __syncthreads();
+  const int before = (w > 0 ? s_w[w - 1] : 0) + x - v;
+  *total = s_w[SP_THREADS / 32 - 1];
+  __syncthreads();
+  return before;
+}
+
+__global__ void __launch_bounds__(SP_THREADS) k_sample_prep(const float* __restrict__ logits, int n, int64_t ld,
+                                                            float temp, float top_p, SampleWs ws,
+                                                            int32_t* __restrict__ out) {
+  __shared__ float s_v[SP_THREADS / 32];
+  __shared__ int s_i[SP_THREADS / 32];
+  const int r = blockIdx.x, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const float* x = logits + (int64_t)r * ld;
+  const int64_t base = (int64_t)r * n;
+
+  // max and its first index (NaN never wins, as in the greedy argmax kernels)
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < n; i += SP_THREADS) sp_merge(bv, bi, x[i], i);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    sp_merge(bv, bi, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o));
+  if (lane == 0) {
+    s_v[w] = bv;
+    s_i[w] = bi;
+  }
+  __syncthreads();
+  bv = s_v[0];
+  bi = s_i[0];
+  for (int k = 1; k < SP_THREADS / 32; ++k) sp_merge(bv, bi, s_v[k], s_i[k]);
+  const int am = bi == 0x7fffffff ? 0 : bi;
+  const float mx = x[am];
+  if (!(temp > 0.f)) {  // greedy
+    if (threadIdx.x == 0) {
+      out[r] = am;
+      ws.cnt[r] = 0;
+      ws.beg[r] = (int)base;
+      ws.end[r] = (int)base;
+      ws.tie[r] = -1;
+    }
+    return;
+  }
+
+  // candidates (not below max - 16) in index order: contiguous ranges per thread
+  const float cutoff = mx - 16.0f;
+  const int per = (n + SP_THREADS - 1) / SP_THREADS;
+  const int i0 = min(n, (int)threadIdx.x * per), i1 = min(n, i0 + per);
+  int mine = 0;
+  for (int i = i0; i < i1; ++i) mine += !(x[i] < cutoff);
+  int C = 0;
+  int off = sp_block_scan(mine, &C);
+  for (int i = i0; i < i1; ++i) {
+    const float l = x[i];
+    if (l < cutoff) continue;
+    ws.cidx[base + off] = i;
+    ws.key_in[base + off] = expf(__fdiv_rn(l - mx, temp));
+    ws.val_in[base + off] = off;
+    ++off;
+  }
+  __syncthreads();  // the CTA's global stores are visible to the CTA after the barrier
+
+  // total in index order: one warp adds the values one by one, 256 per
+  // round, the next round's loads in flight meanwhile
+  if (w == 0) {
+    const float* kp = ws.key_in + base;
+    float total = 0.f;
+    float cur[8], nxt[8];
+    sp_ld8(cur, kp, 0, C);
+    for (int b0 = 0; b0 < C; b0 += 256) {
+      sp_ld8(nxt, kp, b0 + 256, C);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+#pragma unroll
+        for (int j = 0; j < 32; ++j) total += __shfl_sync(0xffffffffu, cur[k], j);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) cur[k] = nxt[k];
+    }
+    if (lane == 0) {
+      ws.target[r] = total * top_p;
+      ws.cnt[r] = C;
+      ws.beg[r] = (int)base;
+      ws.end[r] = (int)(base + C);
+      ws.tie[r] = -1;
+      if (C == 0) out[r] = am;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(32) k_sample_walk(const float* __restrict__ u, int n, SampleWs ws,
+                                                    int32_t* __restrict__ out) {
+  const int r = blockIdx.x, lane = threadIdx.x;
+  const int C = ws.cnt[r];
+  if (C == 0) return;
+  const int64_t base = (int64_t)r * n;
+  const float* ks = ws.key_out + base;
+  float* run = ws.key_in + base;  // running sums (the index-order p are no longer needed)
+  float cum = 0.f;
+  float cur[8], nxt[8];
+  sp_ld8(cur, ks, 0, C);
+  for (int b0 = 0; b0 < C; b0 += 256) {
+    sp_ld8(nxt, ks, b0 + 256, C);
+    float keep[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      keep[k] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        cum += __shfl_sync(0xffffffffu, cur[k], j);
+        if (lane == j) keep[k] = cum;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int e = b0 + 32 * k + lane;
+      if (e < C) run[e] = keep[k];
+      cur[k] = nxt[k];
+    }
+  }
+  __syncwarp();  // the lanes' running sums, visible to lane 0
+  if (lane != 0) return;
+  // the reference picks entry i while the sum before it is < target: the
+  // nucleus is [0, K), K - 1 the first entry whose sum reaches the target
+  const float target = ws.target[r];
+  int lo = 0, hi = C - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (run[mid] >= target) hi = mid;
+    else lo = mid + 1;
+  }
+  const int K = lo + 1;
+  const float rr = u[r] * run[K - 1];
+  lo = 0;
+  hi = K - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (rr <= run[mid]) hi = mid;
+    else lo = mid + 1;
+  }
+  const int pick = lo;  // no sum reaches r (u > 1): the last entry, as the reference
+  const float pp = ks[pick];
+  const bool shared = (pick > 0 && ks[pick - 1] == pp) || (pick + 1 < C && ks[pick + 1] == pp);
+  if (!shared) {
+    out[r] = ws.cidx[base + ws.val_out[base + pick]];
+  } else {
+    ws.tie[r] = pick;
+  }
+}
+
+// The reference's list, replayed up to nucleus entry `pick`.  Entries leave
+// in descending p; among equal p the one at the lowest list position goes
+// first; a removal moves the list's last entry into the freed position.
+// Within a group of equal p: the members' positions are bits of a bitmap,
+// taken in ascending order; when a removal moves a member from the list's
+// end into the freed position (lower than every other member's), that member
+// goes next.  Every step is O(1) apart from the bitmap scan, which only moves
+// forward within a group.
+__global__ void __launch_bounds__(256) k_sample_ties(int n, SampleWs ws, int32_t* __restrict__ out) {
+  const int r = blockIdx.x;
+  const int pick = ws.tie[r];
+  if (pick < 0) return;
+  const int C = ws.cnt[r];
+  const int64_t base = (int64_t)r * n;
+  int* at = reinterpret_cast<int*>(ws.key_in + base);  // list position -> candidate
+  int* pos = ws.val_in + base;                         // candidate -> list position
+  int* tag = ws.aux + 2 * base;                        // candidate -> group tag (group start + 1)
+  uint32_t* bits = reinterpret_cast<uint32_t*>(tag + n);  // list positions of the group's members
+  const int nw = (C + 31) / 32;
+  for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    at[i] = i;
+    pos[i] = i;
+    tag[i] = 0;
+  }
+  for (int i = threadIdx.x; i < nw; i += blockDim.x) bits[i] = 0u;
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  const float* ks = ws.key_out + base;
+  const int* vs = ws.val_out + base;
+  int len = C, sel = 0, s = 0;
+  while (s < C) {
+    const float p = ks[s];
+    int e = s + 1;
+    while (e < C && ks[e] == p) ++e;
+    const int tg = s + 1;
+    for (int q = s; q < e; ++q) {
+      const int c = vs[q];
+      tag[c] = tg;
+      bits[pos[c] >> 5] |= 1u << (pos[c] & 31);
+    }
+    int wcur = 0, carry = -1;
+    for (int k = s; k < e; ++k) {
+      int c = carry;
+      carry = -1;
+      if (c < 0) {  // the lowest marked position
+        while (wcur < nw && bits[wcur] == 0u) ++wcur;
+        if (wcur == nw) {  // cannot happen: the group's members are marked or carried
+          out[r] = ws.cidx[base + vs[pick]];
+          return;
+        }
+        const int bpos = wcur * 32 + __ffs(bits[wcur]) - 1;
+        bits[wcur] &= bits[wcur] - 1u;
+        c = at[bpos];
+      }
+      if (sel == pick) {
+        out[r] = ws.cidx[base + c];
+        ws.tie[r] = -1;
+        return;
+      }
+      const int b = pos[c], last = at[len - 1];
+      if (last != c) {
+        at[b] = last;
+        pos[last] = b;
+        if (tag[last] == tg) {  // a member leaves the end: it is now the lowest
+          bits[(len - 1) >> 5] &= ~(1u << ((len - 1) & 31));
+          carry = last;
+        }
+      }
+      --len;
+      ++sel;
+    }
+    s = e;
+  }
+}
+
+// scratch bytes for R rows of n logits, CUB's temporary storage included
+static int sample_ws_bytes(int R, int n, size_t* cub_bytes, size_t* total) {
+  size_t cb = 0;
+  Q8_CUDA(cub::DeviceSegmentedRadixSort::SortPairsDescending(
+      nullptr, cb, (const float*)nullptr, (float*)nullptr, (const int*)nullptr, (int*)nullptr, R * n, R,
+      (const int*)nullptr, (const int*)nullptr, 0, 32, (cudaStream_t)0));
+  const size_t arr = ((size_t)R * n * 4 + 255) & ~(size_t)255;
+  const size_t rows = ((size_t)R * 4 + 255) & ~(size_t)255;
+  *cub_bytes = cb;
+  *total = 7 * arr + 5 * rows + ((cb + 255) & ~(size_t)255);
+  return Q8_OK;
+}
+
+static SampleWs sample_ws_carve(void* p, int R, int n, void** cub_tmp) {
+  const size_t arr = ((size_t)R * n * 4 + 255) & ~(size_t)255;
+  const size_t rows = ((size_t)R * 4 + 255) & ~(size_t)255;
+  uint8_t* q = static_cast<uint8_t*>(p);
+  SampleWs ws{};
+  ws.cidx = (int*)q; q += arr;
+  ws.key_in = (float*)q; q += arr;
+  ws.val_in = (int*)q; q += arr;
+  ws.key_out = (float*)q; q += arr;
+  ws.val_out = (int*)q; q += arr;
+  ws.beg = (int*)q; q += rows;
+  ws.end = (int*)q; q += rows;
+  ws.cnt = (int*)q; q += rows;
+  ws.target = (float*)q; q += rows;
+  ws.tie = (int*)q; q += rows;
+  ws.aux = (int*)q; q += 2 * arr;
+  *cub_tmp = q;
+  return ws;
+}
+
+size_t sample_scratch_bytes(int rows, int n) {
+  size_t cb = 0, tot = 0;
+  if (sample_ws_bytes(rows, n, &cb, &tot) != Q8_OK) return 0;
+  return tot;
+}
+
+int sample_launch(const float* logits, int rows, int n, int64_t ld, float temp, float top_p, const float* u,
+                  int32_t* out, void* scratch, size_t scratch_bytes, cudaStream_t st) {
+  Q8_CHECK_ARG(rows >= 0 && n >= 1 && ld >= n && (int64_t)rows * n < ((int64_t)1 << 31),
+               "sample: bad shape rows=%d n=%d ld=%lld", rows, n, (long long)ld);
+  if (rows == 0) return Q8_OK;
+  size_t cb = 0, tot = 0;
+  Q8_TRY(sample_ws_bytes(rows, n, &cb, &tot));
+  Q8_CHECK_ARG(scratch && scratch_bytes >= tot, "sample: scratch of %zu bytes, %zu needed", scratch_bytes, tot);
+  void* cub_tmp = nullptr;
+  const SampleWs ws = sample_ws_carve(scratch, rows, n, &cub_tmp);
+  k_sample_prep<<<rows, SP_THREADS, 0, st>>>(logits, n, ld, temp, top_p, ws, out);
+  Q8_TRY(launch_check("k_sample_prep"));
+  if (!(temp > 0.f)) return Q8_OK;
+  Q8_CUDA(cub::DeviceSegmentedRadixSort::SortPairsDescending(cub_tmp, cb, ws.key_in, ws.key_out, ws.val_in,
+                                                             ws.val_out, rows * n, rows, ws.beg, ws.end, 0, 32,
+                                                             st));
+  k_sample_walk<<<rows, 32, 0, st>>>(u, n, ws, out);
+  Q8_TRY(launch_check("k_sample_walk"));
+  k_sample_ties<<<rows, 256, 0, st>>>(n, ws, out);
+  return launch_check("k_sample_ties");
+}
+
+}  // namespace q8
+
+using namespace q8;
+
+extern "C" int q8op_sample(const float* logits, int64_t rows, int64_t n, int64_t ld, float temp, float top_p,
+                           const float* u, int32_t* out, void* stream) {
+  Q8_CHECK_ARG(logits && out && (u || !(temp > 0.f)), "q8op_sample: null pointer");
+  // temp NaN would sample with NaN weights; top_p <= 0 leaves the reference's
+  // nucleus empty (it then indexes an empty list)
+  Q8_CHECK_ARG(!isnan(temp) && (!(temp > 0.f) || top_p > 0.f), "q8op_sample: temp must not be NaN, top_p must be > 0");
+  Q8_CHECK_ARG(rows >= 0 && n >= 1 && ld >= n && rows * n < ((int64_t)1 << 31), "q8op_sample: bad shape");
+  if (rows == 0) return Q8_OK;
+  const size_t need = sample_scratch_bytes((int)rows, (int)n);
+  Q8_CHECK_ARG(need > 0, "q8op_sample: scratch size query failed");
+  void* scr = nullptr;
+  Q8_TRY(op_scratch(need, &scr));
+  return sample_launch(logits, (int)rows, (int)n, ld, temp, top_p, u, out, scr, need, (cudaStream_t)stream);
+}

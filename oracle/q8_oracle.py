@@ -18,6 +18,9 @@ It restates, in numpy, the reference algorithm of plutonium-guy/lama32_mojo:
 * SwiGLU + residual                scripts/gen_oracle.py:90-95
 * layer / cached decode loop       qwen3_mojo/scripts/bench_python.py:96-130
 * final norm + (un)tied lm_head    scripts/gen_oracle.py:126-127, llama31_mojo/scripts/gen_oracle.py:133
+* temperature + nucleus sampling   src/sample.mojo:15-59 (``sample_literal``; no golden
+                                   vectors exist for it: parity unpinned, cross-checked
+                                   against the C restatement ``oracle/q8_ref.c``)
 
 Parity is pinned by ``tests/golden/make_golden.py``, which runs the
 reference's own Python (``pack_q8``, ``gen_oracle.layer``,
@@ -404,6 +407,59 @@ def greedy_generate(model: OracleModel, prompt, steps: int):
         logits = model.forward([t])
         all_logits.append(logits)
     return toks, margins, all_logits
+
+
+def sample_literal(logits, temp: float, top_p: float, u: float) -> int:
+    """sample() of src/sample.mojo:15-59 in float32 scalar steps, loop for loop
+    (pure Python: small rows only); u is the uniform draw the reference takes
+    from random_float64() (:55)."""
+    x = [np.float32(v) for v in np.asarray(logits, np.float32).ravel()]
+
+    def argmax(v):  # :7-12, first maximum
+        best = 0
+        for i in range(1, len(v)):
+            if v[i] > v[best]:
+                best = i
+        return best
+
+    if temp <= 0:
+        return argmax(x)
+    t = np.float32(temp)
+    mx = x[argmax(x)]
+    cutoff = np.float32(mx - np.float32(16.0))
+    cand_idx, cand_p = [], []
+    total = np.float32(0.0)
+    for i, v in enumerate(x):
+        if v < cutoff:
+            continue
+        p = np.float32(np.exp(np.float32(np.float32(v - mx) / t)))
+        cand_idx.append(i)
+        cand_p.append(p)
+        total = np.float32(total + p)
+    if not cand_idx:
+        return argmax(x)
+    target = np.float32(total * np.float32(top_p))
+    nuc_idx, nuc_p = [], []
+    cum = np.float32(0.0)
+    while cum < target and cand_idx:
+        b = 0
+        for i in range(1, len(cand_p)):
+            if cand_p[i] > cand_p[b]:
+                b = i
+        cum = np.float32(cum + cand_p[b])
+        nuc_idx.append(cand_idx[b])
+        nuc_p.append(cand_p[b])
+        cand_idx[b] = cand_idx[-1]
+        cand_p[b] = cand_p[-1]
+        cand_idx.pop()
+        cand_p.pop()
+    r = np.float32(np.float32(u) * cum)
+    acc = np.float32(0.0)
+    for i in range(len(nuc_idx)):
+        acc = np.float32(acc + nuc_p[i])
+        if r <= acc:
+            return nuc_idx[i]
+    return nuc_idx[-1]
 
 
 def rel_l2(a: np.ndarray, b: np.ndarray) -> float:

@@ -15,6 +15,9 @@
  *   q8r_swiglu    k_swiglu_mul   src/llama_common.mojo:476-481
  *   q8r_argmax    k_argmax       src/llama_common.mojo:493-519 (lowest index on ties)
  *   q8r_layer     run_layer_q8   src/llama_q8.mojo:144-230 (one decode token)
+ *   q8r_sample    sample         src/sample.mojo:15-59 (temperature + nucleus, the
+ *                 selection loop literally: repeated first-maximum pick with
+ *                 swap-remove), the uniform draw supplied by the caller
  *
  * Build: oracle/Makefile (gcc -O3 -shared -pthread).  Parallel loops use a
  * small pthread fork/join over rows (no OpenMP runtime in this toolchain).
@@ -267,4 +270,98 @@ void q8r_layer(const q8r_layer_w* w, float* h, int H, int nh, int nkv, int hd, i
   q8r_swiglu(gu, gu + F, F);
   q8r_gemv(gu, 1, F, w->down, H, o);
   for (int i = 0; i < H; ++i) h[i] += o[i];
+}
+
+/* sample (src/sample.mojo:15-59), step by step:
+ *   temp <= 0: greedy argmax (:21-22, first maximum, :7-12);
+ *   candidates: logits >= max - 16, in index order, p = exp((l - max) / temp),
+ *   total = their f32 sum in index order (:23-35); none: argmax (:36-37);
+ *   target = total * top_p; the nucleus is built by picking the largest
+ *   remaining p (first in list order), appending it and moving the list's last
+ *   entry into its place, while cum < target (:38-53);
+ *   r = f32(u) * cum and the first nucleus entry whose running sum reaches r
+ *   (:54-59).  u is the caller's uniform draw (the reference draws
+ *   random_float64()).
+ * margin (may be NULL) receives the smallest relative gap of a decision that
+ * one ulp of exp() could flip: cum against target at the stop, r against the
+ * running sums around the returned entry, and the returned p against the
+ * nearest different candidate p.  A checker whose exp() differs in the last
+ * place may disagree only when that gap is about 1e-6 or less. */
+static double rel_gap(double a, double b) {
+  const double d = fabs(a - b), m = fmax(fabs(a), fabs(b));
+  return m > 0 ? d / m : 0.0;
+}
+
+int q8r_sample(const float* logits, int n, float temp, float top_p, float u, double* margin) {
+  if (margin) *margin = INFINITY;
+  const int am = q8r_argmax(logits, n);
+  if (temp <= 0.0f) return am;
+  const float mx = logits[am];
+  const float cutoff = mx - 16.0f;
+  int* ci = (int*)malloc((size_t)n * sizeof(int));
+  float* cp = (float*)malloc((size_t)n * sizeof(float));
+  int* ni = (int*)malloc((size_t)n * sizeof(int));
+  float* np_ = (float*)malloc((size_t)n * sizeof(float));
+  float* all = (float*)malloc((size_t)n * sizeof(float));
+  int c = 0;
+  float total = 0.0f;
+  for (int i = 0; i < n; ++i) {
+    if (logits[i] < cutoff) continue;
+    const float pr = expf((logits[i] - mx) / temp);
+    ci[c] = i;
+    cp[c] = pr;
+    all[c] = pr;
+    ++c;
+    total += pr;
+  }
+  const int nc = c;
+  int tok = am;
+  if (c > 0) {
+    const float target = total * top_p;
+    int k = 0;
+    float cum = 0.0f, prev = 0.0f;
+    while (cum < target && c > 0) {
+      int b = 0;
+      for (int i = 1; i < c; ++i)
+        if (cp[i] > cp[b]) b = i;
+      prev = cum;
+      cum += cp[b];
+      ni[k] = ci[b];
+      np_[k] = cp[b];
+      ++k;
+      ci[b] = ci[c - 1];
+      cp[b] = cp[c - 1];
+      --c;
+    }
+    double mg = INFINITY;
+    if (margin) {
+      mg = fmin(rel_gap(cum, target), k > 1 ? rel_gap(prev, target) : INFINITY);
+    }
+    const float r = u * cum;
+    float acc = 0.0f, before = 0.0f;
+    int pick = k - 1;
+    for (int i = 0; i < k; ++i) {
+      before = acc;
+      acc += np_[i];
+      if (r <= acc) {
+        pick = i;
+        break;
+      }
+    }
+    tok = ni[pick];
+    if (margin) {
+      mg = fmin(mg, rel_gap(r, acc));
+      if (pick > 0) mg = fmin(mg, rel_gap(r, before));
+      const float pp = np_[pick];
+      for (int i = 0; i < nc; ++i)
+        if (all[i] != pp) mg = fmin(mg, rel_gap(all[i], pp));
+      *margin = mg;
+    }
+  }
+  free(ci);
+  free(cp);
+  free(ni);
+  free(np_);
+  free(all);
+  return tok;
 }

@@ -45,6 +45,8 @@ def lib():
         L.q8r_swiglu.argtypes = [P, P, I]
         L.q8r_argmax.argtypes = [P, I]
         L.q8r_argmax.restype = I
+        L.q8r_sample.argtypes = [P, I, F, F, F, C.POINTER(C.c_double)]
+        L.q8r_sample.restype = I
         L.q8r_layer.argtypes = [C.POINTER(LayerW), P, I, I, I, I, I, F, I, P, P, P, P]
         _lib = L
     return _lib
@@ -62,6 +64,15 @@ def gemv(x: np.ndarray, packed: np.ndarray, m: int) -> np.ndarray:
     y = np.empty((x.shape[0], n), np.float32)
     lib().q8r_gemv(_p(x), x.shape[0], m, _p(packed), n, _p(y))
     return y
+
+
+def sample(logits: np.ndarray, temp: float, top_p: float, u: float):
+    """Token of sample() (src/sample.mojo:15-59) for one logits row and the
+    uniform draw u, with the decision margin (see q8r_sample)."""
+    x = np.ascontiguousarray(logits, np.float32).ravel()
+    mg = C.c_double()
+    tok = lib().q8r_sample(_p(x), x.size, float(temp), float(top_p), float(np.float32(u)), C.byref(mg))
+    return int(tok), float(mg.value)
 
 
 def _rand_packed(rng, n, m):

@@ -1,7 +1,8 @@
 """Tensor parallelism on 2 GPUs: each rank loads the same checkpoint, the
 loader slices its shard (q8_shard_plan), the row-parallel partials are summed
-with NCCL inside the library.  Rank 0's logits, per-layer hidden states and
-greedy tokens must match the single-GPU oracle.  Skipped with fewer than 2 GPUs."""
+inside the library (NCCL for prefill, the one-shot P2P exchange for decode).
+Rank 0's logits, per-layer hidden states, greedy tokens and batched decode
+logits must match the single-GPU oracle.  Skipped with fewer than 2 GPUs."""
 import os
 import socket
 
@@ -47,6 +48,8 @@ def _rank(rank, world, port, cfgname, ids, steps, q):
         out["tokens"] = toks
         m.forward(ids[:3], seq=1)
         out["gen"] = m.generate([toks[0]], [1], 3)[:, 0].tolist()
+        # a batched decode step of both sequences (two token rows per GEMV)
+        _, out["dec_logits"] = m.decode([toks[-1], out["gen"][-1]], [0, 1], logits=True)
         m.close()
         if rank == 0:
             q.put(out)
@@ -55,13 +58,8 @@ def _rank(rank, world, port, cfgname, ids, steps, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("cfgname", ["tiny-llama", "tiny-qwen3", "tiny-llama-untied"])
-def test_tp2_matches_oracle(cuda, cfgname):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+def _run_tp2(cfgname, ids):
     import torch.multiprocessing as mp
-    ocfg = O.PRESETS[cfgname]
-    ids = O.random_ids(ocfg, 9, seed=41)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -76,6 +74,16 @@ def test_tp2_matches_oracle(cuda, cfgname):
             if p.is_alive():
                 p.kill()
     assert all(p.exitcode == 0 for p in procs)
+    return out
+
+
+@pytest.mark.parametrize("cfgname", ["tiny-llama", "tiny-qwen3", "tiny-llama-untied"])
+def test_tp2_matches_oracle(cuda, cfgname):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ocfg = O.PRESETS[cfgname]
+    ids = O.random_ids(ocfg, 9, seed=41)
+    out = _run_tp2(cfgname, ids)
     ck = O.make_q8_checkpoint(ocfg)
     orc = O.OracleModel(ocfg, ck)
     ref = orc.forward(ids)
@@ -93,3 +101,8 @@ def test_tp2_matches_oracle(cuda, cfgname):
         t = o2.forward_argmax([t])
         want.append(t)
     assert out["gen"] == want
+    # batched decode logits: seq 0 next takes toks[-1], seq 1 the last generated token
+    for b, (orc_b, tok) in enumerate([(orc, toks[-1]), (o2, want[-1])]):
+        ref_b = orc_b.forward([tok])
+        got = out["dec_logits"][b]
+        assert O.rel_l2(got, ref_b) < 1e-3 and np.abs(got - ref_b).max() < 2e-2, b

@@ -119,3 +119,37 @@ def test_kv_full_raises():
     m.forward([1, 2, 3])
     with pytest.raises(RuntimeError, match="KV cache full"):
         m.forward([4, 5])
+
+
+def _sample_rows(seed):
+    """Logit rows for the sampler checks: continuous values, planted equal
+    values (ties, a shared maximum), and rows with few distinct values."""
+    rng = np.random.default_rng(seed)
+    rows = []
+    for n, scale in ((50, 3.0), (300, 1.0), (300, 8.0)):
+        rows.append((rng.standard_normal(n) * scale).astype(np.float32))
+    x = (rng.standard_normal(200) * 2).astype(np.float32)
+    x[[5, 17, 90]] = x.max()  # three equal maxima
+    x[[30, 31, 150, 199]] = x[40]
+    rows.append(x)
+    rows.append(rng.integers(-3, 1, 240).astype(np.float32) * np.float32(0.5))  # 4 values, big tie groups
+    return rows
+
+
+def test_sample_c_restatement_matches_literal():
+    """The C restatement of sample() (oracle/q8_ref.c, the GPU checker)
+    agrees with the loop-for-loop Python one on rows with and without ties;
+    a disagreement is only tolerated where one ulp of exp() could flip the
+    decision (margin)."""
+    from oracle import q8_ref as R
+    rng = np.random.default_rng(5)
+    checked = 0
+    for x in _sample_rows(3):
+        for temp in (0.0, -1.0, 0.7, 1.0, 1.8):
+            for top_p in (0.25, 0.9, 1.0):
+                for u in (0.0, float(rng.random()), float(rng.random()), 0.9999999):
+                    want = O.sample_literal(x, temp, top_p, u)
+                    got, margin = R.sample(x, temp, top_p, u)
+                    assert got == want or margin < 1e-6, (temp, top_p, u, got, want, margin)
+                    checked += got == want
+    assert checked > 0.99 * 5 * 5 * 3 * 4
