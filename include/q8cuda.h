@@ -257,6 +257,23 @@ int q8_decode(q8_ctx* ctx, const int32_t* ids, const int32_t* seqs, int B, float
 int q8_generate(q8_ctx* ctx, const int32_t* first_ids, const int32_t* seqs, int B, int steps,
                 int32_t* out_tokens);
 
+/* Temperature + nucleus sampling of every token the context picks — the chat
+ * REPLs' sample(logits, temp, top_p) (src/sample.mojo:15-59) run on the device
+ * right after lm_head, so a chat step needs no logits copy to the host.
+ * temp > 0: q8_forward's argmax output, q8_decode's argmax[] and every
+ * q8_generate step are sampled as q8op_sample does; temp <= 0 (the default)
+ * restores the greedy argmax.  The draw of a row is
+ *   z = seed + (key + 1) * 0x9E3779B97F4A7C15, key = seq << 32 | pos
+ *   z = (z ^ z >> 30) * 0xBF58476D1CE4E5B9; z = (z ^ z >> 27) * 0x94D049BB133111EB;
+ *   z ^= z >> 31;  u = (z >> 40) / 2^24
+ * (SplitMix64's finalizer; pos is the position of the token fed in that row),
+ * so a run is reproducible from the seed.  Synchronizes the context's stream
+ * and drops its captured decode graphs; allocates the sampling scratch (about
+ * 28 bytes per vocabulary entry per sequence) on first use.  top_p must be > 0
+ * when temp > 0.  No counterpart in the reference's GPU path (its sampler runs
+ * on the host over the logits). */
+int q8_set_sampling(q8_ctx* ctx, float temp, float top_p, unsigned long long seed);
+
 /* KV cache state — n_cached (qwen_q8.mojo:69; chat /reset sets it to 0,
  * src/chat.mojo:133-136).  q8_set_n_cached can only shrink. */
 int q8_reset(q8_ctx* ctx, int seq);

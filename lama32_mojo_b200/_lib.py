@@ -77,6 +77,7 @@ SIGNATURES = {
     "q8_set_n_cached": [_P, _I32, _I32],
     "q8_stream": [_P, C.POINTER(_P)],
     "q8_set_profiling": [_P, _I32],
+    "q8_set_sampling": [_P, _F, _F, C.c_uint64],
     "q8_shard_plan": [C.POINTER(q8_config), _I32, _I32, C.c_char_p] + [C.POINTER(_I64)] * 7 + [C.c_char_p, _I32],
     "q8_inspect_checkpoint": [C.c_char_p, C.c_char_p, C.c_size_t, C.POINTER(_I32)],
     "q8_forward_hidden": [_P, _P, _I32, _I32, _I32, _P],

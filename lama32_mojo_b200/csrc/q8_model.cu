@@ -13,6 +13,7 @@
 #include "q8_kernels.h"
 #include "safetensors.h"
 
+#include <cmath>
 #include <fcntl.h>
 #include <nccl.h>
 #include <stdarg.h>
@@ -116,6 +117,24 @@ __global__ void k_argmax_pick(const float* __restrict__ val, const int32_t* __re
 
 // generation step epilogue: feed argmax back as next ids, advance positions,
 // append to the on-device token history.
+// Uniform draw of a sampled row: SplitMix64's finalizer (Steele, Lea, Flood
+// 2014) over seed + (key + 1) * golden gamma, key = sequence << 32 | position
+// of the fed token; the top 24 bits give u in [0, 1) exactly.
+__host__ __device__ inline float q8_draw(unsigned long long seed, int seq, int pos) {
+  const unsigned long long key = ((unsigned long long)(unsigned)seq << 32) | (unsigned)pos;
+  unsigned long long z = seed + (key + 1ull) * 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return (float)(z >> 40) * (1.0f / 16777216.0f);
+}
+
+__global__ void k_sample_draws(const int32_t* __restrict__ pos, const int32_t* __restrict__ seq, int rows,
+                               unsigned long long seed, float* __restrict__ u) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < rows) u[b] = q8_draw(seed, seq[b], pos[b]);
+}
+
 __global__ void k_step_end(const int32_t* __restrict__ amax, int32_t* __restrict__ ids, int32_t* __restrict__ pos,
                            int32_t* __restrict__ hist, int32_t* __restrict__ ctr, int B, int cap) {
   const int b = threadIdx.x;
@@ -205,6 +224,13 @@ struct q8_ctx {
   float *am_val = nullptr, *am_gval = nullptr, *lg_gather = nullptr;
   int32_t *am_idx = nullptr, *am_gidx = nullptr;
   float* logits_host_pin = nullptr;
+  // sampling (q8_set_sampling): temp > 0 replaces the greedy argmax
+  float samp_temp = 0.f, samp_top_p = 1.f;
+  unsigned long long samp_seed = 0;
+  void* samp_ws = nullptr;
+  size_t samp_ws_bytes = 0;
+  float* samp_u = nullptr;       // [rows] uniform draws of the step
+  float* samp_logits = nullptr;  // [rows][V] vocabulary-ordered rows (TP > 1)
 
   std::map<int, cudaGraphExec_t> g_decode, g_gen;
 
@@ -278,7 +304,7 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
   const int nqkv = c->qd + 2 * c->kvd;
   cudaStream_t st = c->st;
   const bool tp = c->tp_size > 1;
-  if (c->mk && !blocks && T <= c->mk_bmax && lrow0 == 0 && lrows == T) {
+  if (c->mk && !blocks && T <= c->mk_bmax && lrow0 == 0 && lrows == T && !(c->samp_temp > 0.f)) {
     MkParams p{};
     p.B = T; p.H = H; p.nh = c->nh; p.nkv = c->nkv; p.hd = c->hd; p.qd = c->qd; p.nqkv = nqkv; p.F = c->F;
     p.V = c->V; p.L = c->cfg.layers; p.eps = c->cfg.eps;
@@ -447,7 +473,29 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
          gemm_dispatch(EPI_STORE, c->xn32, H, c->xs_in, lrows, H, c->lm_head, c->V_loc, c->logits, c->V_loc, nullptr,
                        st));
   }
-  if (!tp) {
+  if (c->samp_temp > 0.f) {  // sampled tokens into argmax_d
+    cudaEvent_t pe;
+    Q8_TRY(prof_begin(c, &pe));
+    const float* lg = c->logits;
+    if (tp) {  // every rank samples the whole vocabulary with the same draws
+      ncclResult_t r = ncclAllGather(c->logits, c->lg_gather, (size_t)lrows * c->V_loc, ncclFloat, c->comm, st);
+      if (r != ncclSuccess) {
+        set_error("logits allgather: %s", ncclGetErrorString(r));
+        return Q8_ERR_COMM;
+      }
+      for (int k = 0; k < c->tp_size; ++k)  // [tp][rows][V_loc] -> [rows][V]
+        Q8_CUDA(cudaMemcpy2DAsync(c->samp_logits + (size_t)k * c->V_loc, (size_t)c->V * 4,
+                                  c->lg_gather + (size_t)k * lrows * c->V_loc, (size_t)c->V_loc * 4,
+                                  (size_t)c->V_loc * 4, lrows, cudaMemcpyDeviceToDevice, st));
+      lg = c->samp_logits;
+    }
+    k_sample_draws<<<ceil_div(lrows, 128), 128, 0, st>>>(c->pos_d + lrow0, c->seq_d + lrow0, lrows, c->samp_seed,
+                                                         c->samp_u);
+    Q8_TRY(launch_check("k_sample_draws"));
+    Q8_TRY(sample_launch(lg, lrows, c->V, c->V, c->samp_temp, c->samp_top_p, c->samp_u, c->argmax_d, c->samp_ws,
+                         c->samp_ws_bytes, st));
+    Q8_TRY(prof_end(c, "sample", (double)lrows * c->V * 4.0));
+  } else if (!tp) {
     PROF(c, "argmax", (double)lrows * c->V * 4.0,
          argmax_launch(c->logits, lrows, c->V, c->V, c->argmax_d, st));
   } else {
@@ -616,7 +664,8 @@ static int destroy_impl(q8_ctx* c) {
                   c->qb_tok0_d, c->qb_len_d, c->argmax_d, c->hist_d, c->ctr_d, c->ticket_d, c->h, c->qkv, c->ypart,
                   c->logits, c->part, c->xs_in, c->xs_ao, c->xs_act, c->xn32, c->ao32, c->act32, c->am_val, c->am_gval, c->lg_gather,
                   c->am_idx, c->am_gidx, c->mk_hB, c->mk_pqkv, c->mk_pres, c->mk_ao, c->mk_act,
-                  c->mk_apart, c->mk_key, c->mk_ticket, c->mk_bar, c->mk_status, c->mk_layers, c->mk_ts, c->mk_ts2};
+                  c->mk_apart, c->mk_key, c->mk_ticket, c->mk_bar, c->mk_status, c->mk_layers, c->mk_ts, c->mk_ts2,
+                  c->samp_ws, c->samp_u, c->samp_logits};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   if (c->pin) cudaFreeHost(c->pin);
@@ -1454,6 +1503,37 @@ int q8_stream(const q8_ctx* ctx, void** stream) {
   Q8_CHECK_ARG(ctx && stream, "q8_stream: null");
   *stream = (void*)ctx->st;
   return Q8_OK;
+}
+
+static int set_sampling_impl(q8_ctx* c, float temp, float top_p, unsigned long long seed) {
+  Q8_CHECK_ARG(c, "q8_set_sampling: null");
+  Q8_CHECK_ARG(!std::isnan(temp) && (!(temp > 0.f) || top_p > 0.f),
+               "q8_set_sampling: temp must not be NaN, top_p must be > 0");
+  Q8_CHECK_ARG((int64_t)c->V_loc * c->tp_size == c->V, "q8_set_sampling: vocabulary shards must tile the vocabulary");
+  Q8_CUDA(cudaSetDevice(c->dev));
+  Q8_CUDA(cudaStreamSynchronize(c->st));
+  // the captured decode steps hold the previous mode and parameters
+  for (auto& kv : c->g_decode) cudaGraphExecDestroy(kv.second);
+  for (auto& kv : c->g_gen) cudaGraphExecDestroy(kv.second);
+  c->g_decode.clear();
+  c->g_gen.clear();
+  if (temp > 0.f && !c->samp_ws) {
+    const int rows = std::max(c->max_seqs, 1);
+    const size_t bytes = sample_scratch_bytes(rows, c->V);
+    Q8_CHECK_ARG(bytes > 0, "q8_set_sampling: scratch size query failed");
+    Q8_TRY(dmalloc(&c->samp_ws, bytes));
+    c->samp_ws_bytes = bytes;
+    Q8_TRY(dmalloc((void**)&c->samp_u, (size_t)rows * 4));
+    if (c->tp_size > 1) Q8_TRY(dmalloc((void**)&c->samp_logits, (size_t)rows * c->V * 4));
+  }
+  c->samp_temp = temp > 0.f ? temp : 0.f;
+  c->samp_top_p = top_p;
+  c->samp_seed = seed;
+  return Q8_OK;
+}
+
+int q8_set_sampling(q8_ctx* ctx, float temp, float top_p, unsigned long long seed) {
+  return fail_ctx(ctx, set_sampling_impl(ctx, temp, top_p, seed));
 }
 
 int q8_set_profiling(q8_ctx* ctx, int on) {

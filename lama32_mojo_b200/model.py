@@ -4,8 +4,9 @@
 src/llama_gpu.mojo:52-170): ``forward(ids) -> logits`` of the last token,
 ``forward_argmax(ids) -> int``, and the read/write ``n_cached`` counter; loading
 is ``load_q8(model_dir, maxlen)`` (``load_qwen_q8`` / ``load_llama``).  It adds
-multi-sequence decode (``decode``), on-device greedy generation
-(``generate``) and tensor parallelism (``tp_rank``/``tp_size``).  All compute
+multi-sequence decode (``decode``), on-device generation (``generate``), device
+sampling (``set_sampling``, the chat REPLs' ``sample``) and tensor parallelism
+(``tp_rank``/``tp_size``).  All compute
 runs in libq8cuda.so; errors raise ``Q8Error`` (``KVCacheFull`` for the
 reference's "KV cache full").
 """
@@ -19,6 +20,20 @@ import numpy as np
 from . import _lib
 from ._lib import check, lib
 from .config import Config, from_model_dir
+
+
+_M64 = (1 << 64) - 1
+
+
+def sample_draw(seed: int, seq: int, pos: int) -> np.float32:
+    """The uniform draw the library uses when sampling the row of sequence
+    ``seq`` whose fed token sits at position ``pos`` (q8_set_sampling)."""
+    key = ((seq & 0xFFFFFFFF) << 32) | (pos & 0xFFFFFFFF)
+    z = (seed + (key + 1) * 0x9E3779B97F4A7C15) & _M64
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & _M64
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & _M64
+    z ^= z >> 31
+    return np.float32((z >> 40) / 16777216.0)
 
 
 def _i32(a) -> np.ndarray:
@@ -123,6 +138,11 @@ class Q8Model:
 
     def reset(self, seq: int = 0):
         self._check(lib().q8_reset(self._ctx, seq))
+
+    def set_sampling(self, temp: float, top_p: float = 1.0, seed: int = 0):
+        """Sample every picked token (temperature + nucleus, src/sample.mojo:15-59)
+        on the device; temp <= 0 restores greedy argmax.  Draws: sample_draw()."""
+        self._check(lib().q8_set_sampling(self._ctx, float(temp), float(top_p), int(seed) & (2**64 - 1)))
 
     # ------------------------------------------------------------------ batched / on-device
     def decode(self, ids: Sequence[int], seqs: Sequence[int], logits: bool = False):

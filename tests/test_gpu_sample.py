@@ -109,3 +109,59 @@ def test_sample_rejects_bad_arguments(cuda):
     st = L.q8op_sample(C.c_void_p(x.data_ptr()), 1, 64, 32, 1.0, 0.9, C.c_void_p(u.data_ptr()),
                        C.c_void_p(out.data_ptr()), None)
     assert st == _lib.Q8_ERR_ARG
+
+
+def _model(cfgname, **kw):
+    from lama32_mojo_b200 import PRESETS
+    from lama32_mojo_b200.model import Q8Model
+    from oracle import q8_oracle as O
+    m = Q8Model(PRESETS[cfgname], **kw)
+    for name, w in O.make_bf16_weights(O.PRESETS[cfgname], 0):
+        m.load_tensor(name, w, packed=False)
+    return m
+
+
+def test_model_sampling_matches_reference_loop(cuda):
+    """q8_set_sampling: the tokens q8_decode / q8_forward / q8_generate pick are
+    sample() of their own logits with the documented per-row draw."""
+    from lama32_mojo_b200.model import sample_draw
+    temp, top_p, seed = 0.8, 0.9, 1234
+    m = _model("tiny-llama", maxlen=64, max_seqs=3)
+    try:
+        for s, p in enumerate(([1, 2, 3, 4], [9, 8, 7], [100, 200, 300, 400, 500])):
+            m.forward(p, seq=s)
+        m.set_sampling(temp, top_p, seed)
+        cur, seqs = [5, 17, 300], [0, 1, 2]
+        for _ in range(3):
+            pos = [m.get_n_cached(s) for s in seqs]
+            am, lg = m.decode(cur, seqs, logits=True)
+            for b in range(3):
+                want, margin = R.sample(lg[b], temp, top_p, sample_draw(seed, seqs[b], pos[b]))
+                assert am[b] == want or margin < 1e-6, (b, am[b], want, margin)
+            cur = [int(t) for t in am]
+        # q8_forward: the last row's token is sampled too
+        ids = np.array([11, 12, 13], np.int32)
+        lg1 = np.empty(m.cfg.vocab, np.float32)
+        tok = np.zeros(1, np.int32)
+        pos0 = m.get_n_cached(1)
+        _lib.check(_lib.lib().q8_forward(m._ctx, ids.ctypes.data, 3, 1, lg1.ctypes.data, tok.ctypes.data))
+        want, margin = R.sample(lg1, temp, top_p, sample_draw(seed, 1, pos0 + 2))
+        assert tok[0] == want or margin < 1e-6
+        # on-device generation: the same state and seed give the same tokens
+        n0 = [m.get_n_cached(s) for s in seqs]
+        g1 = m.generate(cur, seqs, 4)
+        for s in seqs:
+            m.set_n_cached(n0[s], s)
+        g2 = m.generate(cur, seqs, 4)
+        assert np.array_equal(g1, g2)
+        # ... and its first step equals a host-driven step
+        for s in seqs:
+            m.set_n_cached(n0[s], s)
+        am, _ = m.decode(cur, seqs, logits=True)
+        assert list(am) == list(g1[0])
+        # temp <= 0: greedy again
+        m.set_sampling(0.0)
+        am, lg = m.decode([int(t) for t in am], seqs, logits=True)
+        assert list(am) == [int(np.argmax(r)) for r in lg]
+    finally:
+        m.close()

@@ -50,6 +50,10 @@ def _rank(rank, world, port, cfgname, ids, steps, q):
         out["gen"] = m.generate([toks[0]], [1], 3)[:, 0].tolist()
         # a batched decode step of both sequences (two token rows per GEMV)
         _, out["dec_logits"] = m.decode([toks[-1], out["gen"][-1]], [0, 1], logits=True)
+        # device sampling: every rank samples the gathered vocabulary with the same draws
+        m.set_sampling(0.7, 0.9, 5)
+        out["samp_pos"] = [m.get_n_cached(0), m.get_n_cached(1)]
+        out["samp_tok"], out["samp_logits"] = m.decode([3, 4], [0, 1], logits=True)
         m.close()
         if rank == 0:
             q.put(out)
@@ -106,3 +110,8 @@ def test_tp2_matches_oracle(cuda, cfgname):
         ref_b = orc_b.forward([tok])
         got = out["dec_logits"][b]
         assert O.rel_l2(got, ref_b) < 1e-3 and np.abs(got - ref_b).max() < 2e-2, b
+    from lama32_mojo_b200.model import sample_draw
+    from oracle import q8_ref as R
+    for b in range(2):
+        want, margin = R.sample(out["samp_logits"][b], 0.7, 0.9, sample_draw(5, b, out["samp_pos"][b]))
+        assert out["samp_tok"][b] == want or margin < 1e-6, b
