@@ -15,8 +15,8 @@
 //                   in index order (per-thread contiguous ranges + a block
 //                   scan), p, and total summed in index order by one warp
 //                   (256 values per round, the next round's loads in flight);
-//   sort            candidates by p, descending (CUB segmented radix sort,
-//                   one segment per row);
+//   sort            candidates by p, descending (CUB segmented sort, one
+//                   segment per row);
 //   k_sample_walk   one warp per row: the running sums of the sorted p (the
 //                   reference's cum after each pick, and also its second
 //                   loop's acc: the same additions in the same order); the
@@ -32,7 +32,7 @@
 // Values of exp() come from CUDA's expf; the reference uses Mojo's exp.
 #include "q8_kernels.h"
 
-#include <cub/device/device_segmented_radix_sort.cuh>
+#include <cub/device/device_segmented_sort.cuh>
 
 #include <float.h>
 #include <math.h>
@@ -64,6 +64,52 @@ __device__ __forceinline__ void sp_ld8(float (&v)[8], const float* a, int b0, in
     const int e = b0 + 32 * k + lane;
     v[k] = e < C ? a[e] : 0.f;
   }
+}
+
+// Sequential f32 sum of a[0, C) by one warp: the lanes stage 256 values per
+// round in shared memory (coalesced loads, the next round's already in
+// flight), lane 0 adds them one by one.  RUN: the running sums also go to
+// run[0, C).  Returns the sum on every lane.
+template <bool RUN>
+__device__ __forceinline__ float sp_seq_sum(const float* a, int C, float* run, float* sbuf) {
+  const int lane = threadIdx.x & 31;
+  float s = 0.f;
+  float cur[8], nxt[8];
+  sp_ld8(cur, a, 0, C);
+  for (int b0 = 0; b0 < C; b0 += 256) {
+    sp_ld8(nxt, a, b0 + 256, C);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) sbuf[32 * k + lane] = cur[k];
+    __syncwarp();
+    if (lane == 0) {
+      float4* s4 = reinterpret_cast<float4*>(sbuf);
+#pragma unroll 16
+      for (int j = 0; j < 64; ++j) {  // zeros past C leave the sum unchanged
+        float4 v = s4[j];
+        s += v.x;
+        if (RUN) v.x = s;
+        s += v.y;
+        if (RUN) v.y = s;
+        s += v.z;
+        if (RUN) v.z = s;
+        s += v.w;
+        if (RUN) v.w = s;
+        if (RUN) s4[j] = v;
+      }
+    }
+    __syncwarp();
+    if (RUN) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int e = b0 + 32 * k + lane;
+        if (e < C) run[e] = sbuf[32 * k + lane];
+      }
+      __syncwarp();  // read before the next round overwrites the stage
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) cur[k] = nxt[k];
+  }
+  return __shfl_sync(0xffffffffu, s, 0);
 }
 
 __device__ __forceinline__ void sp_merge(float& bv, int& bi, float ov, int oi) {
@@ -156,22 +202,10 @@ __global__ void __launch_bounds__(SP_THREADS) k_sample_prep(const float* __restr
   }
   __syncthreads();  // the CTA's global stores are visible to the CTA after the barrier
 
-  // total in index order: one warp adds the values one by one, 256 per
-  // round, the next round's loads in flight meanwhile
+  // total in index order: one warp adds the values one by one
   if (w == 0) {
-    const float* kp = ws.key_in + base;
-    float total = 0.f;
-    float cur[8], nxt[8];
-    sp_ld8(cur, kp, 0, C);
-    for (int b0 = 0; b0 < C; b0 += 256) {
-      sp_ld8(nxt, kp, b0 + 256, C);
-#pragma unroll
-      for (int k = 0; k < 8; ++k)
-#pragma unroll
-        for (int j = 0; j < 32; ++j) total += __shfl_sync(0xffffffffu, cur[k], j);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) cur[k] = nxt[k];
-    }
+    __shared__ __align__(16) float sbuf[256];
+    const float total = sp_seq_sum<false>(ws.key_in + base, C, nullptr, sbuf);
     if (lane == 0) {
       ws.target[r] = total * top_p;
       ws.cnt[r] = C;
@@ -191,28 +225,8 @@ __global__ void __launch_bounds__(32) k_sample_walk(const float* __restrict__ u,
   const int64_t base = (int64_t)r * n;
   const float* ks = ws.key_out + base;
   float* run = ws.key_in + base;  // running sums (the index-order p are no longer needed)
-  float cum = 0.f;
-  float cur[8], nxt[8];
-  sp_ld8(cur, ks, 0, C);
-  for (int b0 = 0; b0 < C; b0 += 256) {
-    sp_ld8(nxt, ks, b0 + 256, C);
-    float keep[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      keep[k] = 0.f;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        cum += __shfl_sync(0xffffffffu, cur[k], j);
-        if (lane == j) keep[k] = cum;
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int e = b0 + 32 * k + lane;
-      if (e < C) run[e] = keep[k];
-      cur[k] = nxt[k];
-    }
-  }
+  __shared__ __align__(16) float sbuf[256];
+  sp_seq_sum<true>(ks, C, run, sbuf);
   __syncwarp();  // the lanes' running sums, visible to lane 0
   if (lane != 0) return;
   // the reference picks entry i while the sum before it is < target: the
@@ -277,13 +291,30 @@ __global__ void __launch_bounds__(256) k_sample_ties(int n, SampleWs ws, int32_t
     const float p = ks[s];
     int e = s + 1;
     while (e < C && ks[e] == p) ++e;
+    if (e == s + 1) {  // a lone value: no choice to replay
+      const int c = vs[s];
+      if (sel == pick) {  // cannot happen: the pick's group has several members
+        out[r] = ws.cidx[base + c];
+        ws.tie[r] = -1;
+        return;
+      }
+      const int b = pos[c], last = at[len - 1];
+      at[b] = last;
+      pos[last] = b;
+      --len;
+      ++sel;
+      s = e;
+      continue;
+    }
     const int tg = s + 1;
+    int minp = 0x7fffffff;
     for (int q = s; q < e; ++q) {
       const int c = vs[q];
       tag[c] = tg;
       bits[pos[c] >> 5] |= 1u << (pos[c] & 31);
+      minp = min(minp, pos[c]);
     }
-    int wcur = 0, carry = -1;
+    int wcur = minp >> 5, carry = -1;
     for (int k = s; k < e; ++k) {
       int c = carry;
       carry = -1;
@@ -321,9 +352,9 @@ __global__ void __launch_bounds__(256) k_sample_ties(int n, SampleWs ws, int32_t
 // scratch bytes for R rows of n logits, CUB's temporary storage included
 static int sample_ws_bytes(int R, int n, size_t* cub_bytes, size_t* total) {
   size_t cb = 0;
-  Q8_CUDA(cub::DeviceSegmentedRadixSort::SortPairsDescending(
-      nullptr, cb, (const float*)nullptr, (float*)nullptr, (const int*)nullptr, (int*)nullptr, R * n, R,
-      (const int*)nullptr, (const int*)nullptr, 0, 32, (cudaStream_t)0));
+  Q8_CUDA(cub::DeviceSegmentedSort::SortPairsDescending(nullptr, cb, (const float*)nullptr, (float*)nullptr,
+                                                        (const int*)nullptr, (int*)nullptr, R * n, R,
+                                                        (const int*)nullptr, (const int*)nullptr, (cudaStream_t)0));
   const size_t arr = ((size_t)R * n * 4 + 255) & ~(size_t)255;
   const size_t rows = ((size_t)R * 4 + 255) & ~(size_t)255;
   *cub_bytes = cb;
@@ -370,9 +401,8 @@ int sample_launch(const float* logits, int rows, int n, int64_t ld, float temp, 
   k_sample_prep<<<rows, SP_THREADS, 0, st>>>(logits, n, ld, temp, top_p, ws, out);
   Q8_TRY(launch_check("k_sample_prep"));
   if (!(temp > 0.f)) return Q8_OK;
-  Q8_CUDA(cub::DeviceSegmentedRadixSort::SortPairsDescending(cub_tmp, cb, ws.key_in, ws.key_out, ws.val_in,
-                                                             ws.val_out, rows * n, rows, ws.beg, ws.end, 0, 32,
-                                                             st));
+  Q8_CUDA(cub::DeviceSegmentedSort::SortPairsDescending(cub_tmp, cb, ws.key_in, ws.key_out, ws.val_in, ws.val_out,
+                                                        rows * n, rows, ws.beg, ws.end, st));
   k_sample_walk<<<rows, 32, 0, st>>>(u, n, ws, out);
   Q8_TRY(launch_check("k_sample_walk"));
   k_sample_ties<<<rows, 256, 0, st>>>(n, ws, out);
