@@ -12,8 +12,9 @@
 // Every f32 sum above is sequential, so the result depends on the order of
 // the additions; this file keeps each order and each rounding:
 //   k_sample_prep   one CTA per row: max / first argmax, candidates compacted
-//                   in index order (per-thread contiguous ranges + a block
-//                   scan), p, and total summed in index order by one warp
+//                   in index order (contiguous range per warp, read 32 at a
+//                   time, order kept by ballots), p, and total summed in index
+//                   order by one warp
 //                   (256 values per round, the next round's loads in flight);
 //   sort            candidates by p, descending (CUB segmented sort, one
 //                   segment per row);
@@ -119,34 +120,6 @@ __device__ __forceinline__ void sp_merge(float& bv, int& bi, float ov, int oi) {
   }
 }
 
-// exclusive prefix sum of v over the CTA (SP_THREADS threads); *total = sum
-__device__ __forceinline__ int sp_block_scan(int v, int* total) {
-  __shared__ int s_w[SP_THREADS / 32];
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  int x = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
-  }
-  if (lane == 31) s_w[w] = x;
-  __syncthreads();
-  if (w == 0) {
-    int t = s_w[lane];
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, t, o);
-      if (lane >= o) t += y;
-    }
-    s_w[lane] = t;
-  }
-  __syncthreads();
-  const int before = (w > 0 ? s_w[w - 1] : 0) + x - v;
-  *total = s_w[SP_THREADS / 32 - 1];
-  __syncthreads();
-  return before;
-}
-
 __global__ void __launch_bounds__(SP_THREADS) k_sample_prep(const float* __restrict__ logits, int n, int64_t ld,
                                                             float temp, float top_p, SampleWs ws,
                                                             int32_t* __restrict__ out) {
@@ -157,9 +130,20 @@ __global__ void __launch_bounds__(SP_THREADS) k_sample_prep(const float* __restr
   const int64_t base = (int64_t)r * n;
 
   // max and its first index (NaN never wins, as in the greedy argmax kernels)
+  // (eight loads in flight per thread: one CTA streams the whole row)
   float bv = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < n; i += SP_THREADS) sp_merge(bv, bi, x[i], i);
+  for (int i0 = threadIdx.x; i0 < n; i0 += 8 * SP_THREADS) {
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = i0 + k * SP_THREADS;
+      v[k] = i < n ? x[i] : -INFINITY;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (i0 + k * SP_THREADS < n) sp_merge(bv, bi, v[k], i0 + k * SP_THREADS);
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1)
     sp_merge(bv, bi, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o));
@@ -184,21 +168,51 @@ __global__ void __launch_bounds__(SP_THREADS) k_sample_prep(const float* __restr
     return;
   }
 
-  // candidates (not below max - 16) in index order: contiguous ranges per thread
+  // candidates (not below max - 16) in index order: warp w owns the
+  // contiguous range [w L, (w + 1) L), read 32 coalesced values at a time
+  __shared__ int s_cnt[SP_THREADS / 32];
   const float cutoff = mx - 16.0f;
-  const int per = (n + SP_THREADS - 1) / SP_THREADS;
-  const int i0 = min(n, (int)threadIdx.x * per), i1 = min(n, i0 + per);
+  constexpr int NW = SP_THREADS / 32;
+  const int L = (n + NW - 1) / NW;
+  const int i0 = min(n, w * L), i1 = min(n, i0 + L);
   int mine = 0;
-  for (int i = i0; i < i1; ++i) mine += !(x[i] < cutoff);
-  int C = 0;
-  int off = sp_block_scan(mine, &C);
-  for (int i = i0; i < i1; ++i) {
-    const float l = x[i];
-    if (l < cutoff) continue;
-    ws.cidx[base + off] = i;
-    ws.key_in[base + off] = expf(__fdiv_rn(l - mx, temp));
-    ws.val_in[base + off] = off;
-    ++off;
+  for (int b = i0 + lane; b < i1; b += 8 * 32) {
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = b + 32 * k < i1 ? x[b + 32 * k] : -INFINITY;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) mine += b + 32 * k < i1 && !(v[k] < cutoff);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mine += __shfl_xor_sync(0xffffffffu, mine, o);
+  if (lane == 0) s_cnt[w] = mine;
+  __syncthreads();
+  int off = 0, C = 0;
+  for (int k = 0; k < NW; ++k) {  // the warps' offsets, in warp order
+    const int v = s_cnt[k];
+    if (k < w) off += v;
+    C += v;
+  }
+  for (int b0 = i0; b0 < i1; b0 += 8 * 32) {  // uniform per warp: every lane takes part in the ballots
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = b0 + 32 * k + lane;
+      v[k] = i < i1 ? x[i] : -INFINITY;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = b0 + 32 * k + lane;
+      const bool take = i < i1 && !(v[k] < cutoff);
+      const unsigned m = __ballot_sync(0xffffffffu, take);
+      if (take) {
+        const int o = off + __popc(m & ((1u << lane) - 1u));
+        ws.cidx[base + o] = i;
+        ws.key_in[base + o] = expf(__fdiv_rn(v[k] - mx, temp));
+        ws.val_in[base + o] = o;
+      }
+      off += __popc(m);
+    }
   }
   __syncthreads();  // the CTA's global stores are visible to the CTA after the barrier
 
