@@ -326,3 +326,43 @@ def test_persistent_decode_step_matches_per_op(cuda, cfgname, monkeypatch):
     assert r < 1e-5, r
     assert out["1"][1] == out["0"][1]
     assert O.rel_l2(out["1"][2], out["0"][2]) < 1e-5
+
+
+def test_batched_decode_matches_single_sequence_wide(cuda):
+    """Hidden 4096 (Llama-3.1-8B width, one layer): decode batches of 3 and 6
+    sequences (split-f16 GEMVs with the RMSNorm in front) must give the logits
+    of per-sequence decode (the digit GEMV, one token per launch) to f32
+    accuracy, and the same greedy tokens."""
+    import torch
+
+    from lama32_mojo_b200.config import Config
+    cfg = Config("wide-1l", 4096, 1, 32, 8, 128, 1024, 512, 1e-5, 500000.0, "llama3", 8.0, 1.0, 4.0, 8192.0,
+                 False, False)
+    m = Q8Model(cfg, maxlen=32, max_seqs=6, max_tokens=64)
+    try:
+        g = torch.Generator(device=cuda).manual_seed(21)
+        for name in cfg.weight_names():
+            shape = cfg.tensor_shape(name)
+            if len(shape) == 2:
+                w = (torch.randn(shape, generator=g, device=cuda) * 0.02).to(torch.bfloat16)
+            else:
+                w = torch.ones(shape, device=cuda, dtype=torch.bfloat16)
+            m.load_tensor(name, w, packed=False)
+        torch.cuda.synchronize()
+        rng = np.random.default_rng(22)
+        seqs = list(range(6))
+        for s in seqs:
+            m.forward(rng.integers(0, cfg.vocab, 3 + s).tolist(), seq=s)
+        n0 = [m.get_n_cached(s) for s in seqs]
+        ids = rng.integers(0, cfg.vocab, 6).tolist()
+        for B in (6, 3):
+            am, lg = m.decode(ids[:B], seqs[:B], logits=True)
+            for b in range(B):
+                m.set_n_cached(n0[b], b)
+                am1, lg1 = m.decode([ids[b]], [b], logits=True)
+                assert O.rel_l2(lg[b], lg1[0]) < 1e-5, (B, b)
+                assert int(am[b]) == int(am1[0])
+            for b in range(B):
+                m.set_n_cached(n0[b], b)
+    finally:
+        m.close()
