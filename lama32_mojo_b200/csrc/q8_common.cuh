@@ -139,16 +139,22 @@ static __device__ int g_q8_device_error;
 
 // Bounded wait on a barrier phase: gives up after ~2^31 cycles (about a
 // second), records Q8_ERR_TIMEOUT in g_q8_device_error and returns false, so
-// a lost completion never hangs the GPU.
+// a lost completion never hangs the GPU.  The error word (another wait gave
+// up: return so the grid drains) is read every 2^20 cycles of waiting, not
+// on entry: a global load there would add its latency to every wait.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
-  // once any wait has given up, later ones return at once so the grid drains
-  if (*reinterpret_cast<volatile int*>(&g_q8_device_error)) return false;
   const long long t0 = clock64();
+  long long next = t0 + (1ll << 20);
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > (1ll << 31)) {
-      atomicExch(&g_q8_device_error, Q8_ERR_TIMEOUT);
-      return false;
+    const long long t = clock64();
+    if (t > next) {
+      if (*reinterpret_cast<volatile int*>(&g_q8_device_error)) return false;
+      if (t - t0 > (1ll << 31)) {
+        atomicExch(&g_q8_device_error, Q8_ERR_TIMEOUT);
+        return false;
+      }
+      next = t + (1ll << 20);
     }
   }
   return true;
