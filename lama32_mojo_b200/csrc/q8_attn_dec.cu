@@ -540,11 +540,29 @@ static int ad_dispatch(const AdArgs& a, const CUtensorMap& tm, int hd, dim3 grid
   return Q8_ERR_ARG;
 }
 
+// Context splits per (token, kv head): one CTA per SM at a time, so the
+// launch takes ceil(items * ns / SMs) waves of CTAs that each stream maxlen /
+// ns positions after a fixed cost (launch, prologue, split merge) worth about
+// AD_FIXED_KEYS positions; ns minimises waves x (AD_FIXED_KEYS + maxlen / ns).
+// Batch 1 of 8 kv heads gets 18 splits (one wave), batch 64 gets 2 (seven
+// nearly full waves instead of 3.5).
+constexpr int AD_FIXED_KEYS = 300;
+
 int attention_decode_nsplit(int items, int maxlen) {
-  int ns = num_sms() / std::max(1, items);
-  ns = std::min(ns, (maxlen + AD_KB - 1) / AD_KB);
-  ns = std::min(ns, AD_MAXSPLIT);
-  return std::max(1, ns);
+  items = std::max(1, items);
+  const int sms = num_sms();
+  const int nmax = std::max(1, std::min(AD_MAXSPLIT, (maxlen + AD_KB - 1) / AD_KB));
+  int best = 1;
+  double best_cost = 1e300;
+  for (int ns = 1; ns <= nmax; ++ns) {
+    const double waves = (double)ceil_div((int64_t)items * ns, sms);
+    const double cost = waves * (AD_FIXED_KEYS + (double)maxlen / ns);
+    if (cost < best_cost * (1.0 - 1e-9)) {
+      best_cost = cost;
+      best = ns;
+    }
+  }
+  return best;
 }
 
 size_t attention_decode_part_floats(int T, int nkv, int nsplit, int group, int hd) {
