@@ -163,6 +163,24 @@ class Q8Model:
         self._check(lib().q8_generate(self._ctx, first.ctypes.data, seqs.ctypes.data, B, steps, out.ctypes.data))
         return out
 
+    def chat_generate(self, ids: Sequence[int], temp: float = 0.0, top_p: float = 1.0, eos: int = -1,
+                      seed: int = 0, max_new: Optional[int] = None, seq: int = 0) -> list:
+        """One assistant turn of the chat REPLs' generate() (qwen3_mojo/src/chat_q8.mojo:53-97,
+        src/chat.mojo): prefill ``ids`` after the cached context, then one token per
+        forward until ``eos`` or a full context (n_cached == maxlen), each token
+        picked on the device (greedy for temp <= 0, else sample() with ``top_p``
+        and draws from ``seed``).  Returns the tokens produced; ``eos`` is not
+        included.  ``max_new`` optionally caps the count."""
+        self.set_sampling(temp, top_p, seed)
+        out = []
+        nxt = self.forward_argmax(ids, seq)
+        while self.get_n_cached(seq) < self.maxlen:
+            if nxt == eos or (max_new is not None and len(out) >= max_new):
+                break
+            out.append(nxt)
+            nxt = self.forward_argmax([nxt], seq)
+        return out
+
     @property
     def stream(self) -> int:
         p = C.c_void_p()

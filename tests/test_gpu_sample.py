@@ -165,3 +165,30 @@ def test_model_sampling_matches_reference_loop(cuda):
         assert list(am) == [int(np.argmax(r)) for r in lg]
     finally:
         m.close()
+
+
+def test_chat_generate_mirrors_the_repl_loop(cuda):
+    """Q8Model.chat_generate: greedy turns equal the oracle's greedy tokens, stop
+    before EOS, stop when the context is full; sampled turns repeat for a seed."""
+    from oracle import q8_oracle as O
+    m = _model("tiny-llama", maxlen=24, max_seqs=1)
+    try:
+        prompt = [3, 1, 4, 1, 5]
+        want = O.greedy_generate(O.OracleModel(O.PRESETS["tiny-llama"], O.make_q8_checkpoint(O.PRESETS["tiny-llama"])),
+                                 prompt, 5)[0]
+        got = m.chat_generate(prompt, temp=0.0, max_new=6)
+        assert got == want[:6], (got, want)
+        m.reset()
+        eos = want[3]
+        stop = want.index(eos)  # the first occurrence ends the turn
+        assert m.chat_generate(prompt, temp=0.0, eos=eos) == want[:stop]
+        m.reset()
+        full = m.chat_generate(prompt, temp=0.0)  # no EOS: runs until the context is full
+        assert m.n_cached == 24 and len(full) == 24 - len(prompt)
+        m.reset()
+        a = m.chat_generate(prompt, temp=0.8, top_p=0.9, seed=9, max_new=8)
+        m.reset()
+        b = m.chat_generate(prompt, temp=0.8, top_p=0.9, seed=9, max_new=8)
+        assert a == b and len(a) == 8
+    finally:
+        m.close()
