@@ -5,7 +5,7 @@
 // (src/llama_common.mojo:476):
 //   y[m, n] (+)= sum_k x16[m, k] * f16(q[n, k] * s[n, k/64])
 //
-// Tile: 128 weight rows (MMA M) x BN tokens (MMA N, 128 or 256), K in steps
+// Tile: 128 weight rows (MMA M) x BN tokens (MMA N: 64, 128 or 256), K in steps
 // of 64 (one quantization group).  Warp roles (320 threads):
 //   warp 0     TMA producer: two int8 code boxes [64 rows x 64 B] (no swizzle)
 //              and the f16 activation box [BN tokens x 128 B] (128 B swizzle)
@@ -513,6 +513,9 @@ static int tc_attr() {
 
 template <bool X>
 static int tc_attr_all() {
+  Q8_TRY((tc_attr<EPI_STORE, 64, X>()));
+  Q8_TRY((tc_attr<EPI_ADD, 64, X>()));
+  Q8_TRY((tc_attr<EPI_SWIGLU, 64, X>()));
   Q8_TRY((tc_attr<EPI_STORE, 128, X>()));
   Q8_TRY((tc_attr<EPI_ADD, 128, X>()));
   Q8_TRY((tc_attr<EPI_SWIGLU, 128, X>()));
@@ -536,16 +539,19 @@ static int tc_init() {
   if (done[dev & 63]) return Q8_OK;
   Q8_TRY(tc_attr_all<false>());
   Q8_TRY(tc_attr_all<true>());
-  if (cudaMalloc(&g_tc_ws[dev & 63], (size_t)TC_WS_TILES * TC_BM * 128 * 4) != cudaSuccess ||
-      cudaMalloc(&g_tc_tickets[dev & 63], (size_t)TC_WS_TILES * 4) != cudaSuccess ||
-      cudaMemset(g_tc_tickets[dev & 63], 0, (size_t)TC_WS_TILES * 4) != cudaSuccess) {
+  cudaError_t e = cudaMalloc(&g_tc_ws[dev & 63], (size_t)TC_WS_TILES * TC_BM * 128 * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&g_tc_tickets[dev & 63], (size_t)TC_WS_TILES * 4);
+  if (e == cudaSuccess) e = cudaMemset(g_tc_tickets[dev & 63], 0, (size_t)TC_WS_TILES * 4);
+  if (e != cudaSuccess) {
     cudaGetLastError();
-    set_error("gemm_tc: split-K workspace allocation failed");
-    return Q8_ERR_OOM;
+    set_error("gemm_tc: split-K workspace allocation failed: %s", cudaGetErrorString(e));
+    return e == cudaErrorMemoryAllocation ? Q8_ERR_OOM : Q8_ERR_CUDA;
   }
   done[dev & 63] = true;
   return Q8_OK;
 }
+
+int gemm_tc_prepare() { return tc_init(); }
 
 template <int BN, bool X>
 static void tc_launch(int epi, dim3 grid, const CUtensorMap& tmc, const CUtensorMap& tmx, const CUtensorMap& tmxl,
@@ -599,8 +605,9 @@ int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int64_t x16lo, int 
   const int64_t rb = q8_row_bytes(K);
   const int wrows = epi == EPI_SWIGLU ? 2 * N : N;
   const bool X = x16lo > 0;
-  // 256-token tiles halve the dequantization work per MMA
-  const int bn = M >= 256 ? 256 : 128;
+  // 256-token tiles halve the dequantization work per MMA; decode batches of
+  // <= 64 tokens take 64-token tiles (half the MMA work of a mostly empty 128)
+  const int bn = M >= 256 ? 256 : (M <= 64 ? 64 : 128);
   CUtensorMap tmc, tmx, tmxl;
   {
     // codes of every row: K bytes after the K/32 bytes of f16 group scales
@@ -625,7 +632,7 @@ int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int64_t x16lo, int 
   {
     const int ntile = (int)(grid.x * grid.y), nkb = K / (8 * TC_BK);
     int ks = 1;
-    if (bn == 128 && ntile < num_sms()) ks = std::min(nkb, std::max(1, num_sms() / ntile));
+    if (bn <= 128 && ntile < num_sms()) ks = std::min(nkb, std::max(1, num_sms() / ntile));
     while (ks > 1 && ntile * ks > TC_WS_TILES) --ks;
     if (ks > 1) {
       int dev = 0;
@@ -637,8 +644,10 @@ int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int64_t x16lo, int 
     }
   }
   if (X && bn == 256) tc_launch<256, true>(epi, grid, tmc, tmx, tmxl, p, st);
+  else if (X && bn == 64) tc_launch<64, true>(epi, grid, tmc, tmx, tmxl, p, st);
   else if (X) tc_launch<128, true>(epi, grid, tmc, tmx, tmxl, p, st);
   else if (bn == 256) tc_launch<256, false>(epi, grid, tmc, tmx, tmxl, p, st);
+  else if (bn == 64) tc_launch<64, false>(epi, grid, tmc, tmx, tmxl, p, st);
   else tc_launch<128, false>(epi, grid, tmc, tmx, tmxl, p, st);
   return launch_check("k_gemm_q8_tc");
 }

@@ -43,6 +43,8 @@ int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int64_t x16lo, int 
                    float* y, int64_t ldy, __half* y16, int64_t ldy16, int64_t y16lo, cudaStream_t st);
 // After a synchronize: Q8_OK, or the timeout a pipeline wait recorded (cleared).
 int gemm_tc_poll_error();
+// Kernel attributes and the per-device split-K workspace (outside stream capture).
+int gemm_tc_prepare();
 // Smallest token batch the model runtime sends to the tensor-core GEMM.
 constexpr int kTcMinTokens = 128;
 // token count from which batches use the tensor-core GEMM (Q8_TC_MIN, default kTcMinTokens)

@@ -880,6 +880,9 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
     return bail((set_error("cudaMallocHost failed"), Q8_ERR_OOM));
 
   if ((s = argmax_prepare())) return bail(s);
+  // the tensor-core GEMM's kernel attributes and split-K workspace, before
+  // any decode step is captured into a graph (no allocation during capture)
+  if (c->tc && (s = gemm_tc_prepare())) return bail(s);
   // digit GEMV scratch (split-tile partials, tickets): sized here, outside any
   // stream capture
   if ((s = gemv_d_prepare(std::max({ceil_div(c->qd + 2 * c->kvd, 16), ceil_div(H, 16), ceil_div(c->F, 8),
