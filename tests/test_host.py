@@ -171,3 +171,50 @@ def test_inspect_rejects_truncated_and_corrupt(tmp_path):
         M.inspect_checkpoint(str(tmp_path))
     with pytest.raises(_lib.Q8Error):
         M.inspect_checkpoint(str(tmp_path / "nope"))
+
+
+class _StubModel:
+    """Stands in for the device model behind Q8Model.chat_generate: a fixed
+    token script, a KV counter and the sampling settings it was given."""
+
+    def __init__(self, script, maxlen):
+        self.script, self.maxlen, self.n, self.calls, self.sampling = list(script), maxlen, 0, [], None
+
+    def set_sampling(self, temp, top_p, seed):
+        self.sampling = (temp, top_p, seed)
+
+    def forward_argmax(self, ids, seq=0):
+        self.calls.append(list(ids))
+        self.n += len(ids)
+        return self.script[len(self.calls) - 1]
+
+    def get_n_cached(self, seq=0):
+        return self.n
+
+
+def _chat(stub, ids, **kw):
+    return M.Q8Model.chat_generate(stub, ids, **kw)
+
+
+def test_chat_generate_control_flow():
+    """The REPL loop of chat_q8.mojo:53-97: stop before EOS, stop at a full
+    context, feed each token back, pass the sampling settings through."""
+    s = _StubModel([7, 8, 9, 2, 5, 6], maxlen=100)
+    assert _chat(s, [1, 2, 3], temp=0.6, top_p=0.9, eos=2, seed=4) == [7, 8, 9]
+    assert s.calls == [[1, 2, 3], [7], [8], [9]] and s.sampling == (0.6, 0.9, 4)
+    s = _StubModel([7, 8, 9, 10, 11, 12, 13], maxlen=6)  # 3 prompt tokens + 3 steps fill it
+    assert _chat(s, [1, 2, 3]) == [7, 8, 9] and s.n == 6
+    s = _StubModel([7, 8, 9, 10, 11], maxlen=100)
+    assert _chat(s, [1], max_new=2) == [7, 8]
+    s = _StubModel([2], maxlen=100)
+    assert _chat(s, [1], eos=2) == []
+
+
+def test_sample_draw_is_uniform_24_bit():
+    """The model's per-row draws: 24-bit values in [0, 1), reproducible, and
+    different for neighbouring sequences and positions."""
+    d = [M.sample_draw(5, s, p) for s in range(4) for p in range(256)]
+    assert all(0.0 <= v < 1.0 and float(v) * 2 ** 24 == int(float(v) * 2 ** 24) for v in d)
+    assert len(set(d)) == len(d)
+    assert M.sample_draw(5, 1, 7) == M.sample_draw(5, 1, 7) != M.sample_draw(6, 1, 7)
+    assert 0.4 < float(np.mean(d)) < 0.6
