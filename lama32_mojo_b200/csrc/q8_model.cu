@@ -174,7 +174,7 @@ struct q8_ctx {
   int qb_max = 1;
   cudaStream_t st = nullptr;
   ncclComm_t comm = nullptr;
-  int tc_dmin = 32;        // decode batches from this size run the tensor-core pipeline
+  int tc_dmin = 16;        // decode batches from this size run the tensor-core pipeline
   ArState ar;             // one-shot P2P allreduce for decode (TP > 1)
   int* ar_status_pin = nullptr;
   std::string err;
@@ -745,7 +745,7 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
     // Q8_TC_DECODE_MIN: decode batches from this many sequences use the
     // tensor-core pipeline (default 32; the GEMV kernels below it)
     const char* d = getenv("Q8_TC_DECODE_MIN");
-    c->tc_dmin = d ? std::max(1, atoi(d)) : 32;
+    c->tc_dmin = d ? std::max(1, atoi(d)) : 16;
   }
   c->V = C.vocab;
   c->V_loc = C.vocab / tp_size;
