@@ -116,20 +116,36 @@ def cpu_baseline(cfg, batch: int, ctx: int, layers: int, steps: int = 2):
     return r
 
 
+PROFILED_STEPS = 4  # decode steps run with per-launch profiling after the timed region
+
+
+def workload(a, world: int):
+    """The decode workload both arms report: prompt length, the context at the
+    middle of the timed steps, and the config object of the JSON line."""
+    prompt = a.ctx - a.warmup - a.steps - a.e2e_steps - 8
+    ctx_mid = prompt + a.warmup + a.steps // 2
+    config = {"workload": f"{a.model} Q8 greedy decode, batch {a.batch}, KV capacity {a.ctx}, "
+                          f"context {prompt}..{prompt + a.warmup + a.steps + a.e2e_steps + PROFILED_STEPS}",
+              "model": a.model, "global_batch": a.batch, "seq_len": a.ctx, "prompt": prompt,
+              "parallelism": f"tp{world}", "kv_dtype": "f32",
+              "l2": "weights+KV per step > 126 MB L2 (no flush needed)"}
+    return prompt, ctx_mid, config
+
+
 def run_reference_arm(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     from lama32_mojo_b200.config import PRESETS
     cfg = PRESETS[a.model]
-    ctx = a.ctx - 128
+    # the same workload as the GPU arm, sampled at the middle of its timed steps
+    _, ctx, config = workload(a, a.gpus)
     r = cpu_baseline(cfg, a.batch, ctx, a.cpu_layers, steps=max(1, min(a.steps, 3)))
     line = {
         "impl": "reference", "metric": "decode tok/s", "value": r["tok_s"], "unit": "tok/s",
         "n_gpus": a.gpus, "steps": r["steps"], "warmup": 1, "ms_per_step": r["ms_per_step"],
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": f"{a.model} Q8 decode batch {a.batch} at ctx {ctx}",
-                                        "model": a.model, "global_batch": a.batch, "seq_len": ctx},
+        "data": "synthetic", "config": config,
         "cpu_baseline": {"value": r["tok_s"], "unit": "tok/s", "cores": r["threads"], "kind": "port",
                          "sample": r["sample"]},
         "e2e": {"value": r["tok_s"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -168,7 +184,7 @@ def main():
 
     cfg = PRESETS[a.model]
     B = a.batch
-    prompt = a.ctx - a.warmup - a.steps - a.e2e_steps - 8
+    prompt, ctx_mid, config = workload(a, world)
     assert prompt > 0, "ctx too small for warmup+steps"
     m = load_synthetic(cfg, device=local, seed=0, maxlen=a.ctx, max_seqs=B, max_tokens=2048,
                        tp_rank=rank, tp_size=world, nccl_id=nid)
@@ -245,7 +261,7 @@ def main():
     # ---- roofline of the dominant kernel (Q8 GEMV), per-launch CUDA events
     m.set_profiling(True)
     agg = {}
-    nprof = 4
+    nprof = PROFILED_STEPS
     for _ in range(nprof):
         cur = m.decode(cur, seqs).tolist()
         for k, (kms, kb, kl) in m.profile().items():
@@ -300,7 +316,6 @@ def main():
                "gemm_mode": "split operands (hi*hi + hi*lo + lo*hi tcgen05 MMAs, f32-accurate)",
                "share": {k: round(v[0] / tot_ms, 3) for k, v in pprof.items()} if tot_ms > 0 else None}
 
-    ctx_mid = prompt + a.warmup + a.steps // 2
     step_bytes = cfg.decode_bytes(B, ctx_mid, tp=world)
 
     cpu = None
@@ -318,11 +333,7 @@ def main():
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_per_step, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8xf32",
             "data": "synthetic (random-init N(0,0.02) weights, random prompt ids)",
-            "config": {"workload": f"{a.model} Q8 greedy decode, batch {B}, KV capacity {a.ctx}, "
-                                   f"context {prompt}..{prompt + a.warmup + a.steps + a.e2e_steps + nprof}",
-                       "model": a.model, "global_batch": B, "seq_len": a.ctx, "prompt": prompt,
-                       "parallelism": f"tp{world}", "kv_dtype": "f32",
-                       "l2": "weights+KV per step > 126 MB L2 (no flush needed)"},
+            "config": config,
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 12 * B,
                     "d2h_bytes_per_step": 4 * B},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
