@@ -5,7 +5,7 @@
  * Drop-in boundary for plutonium-guy/lama32_mojo's Q8 path.  Each entry point
  * names the reference interface it replaces (paths relative to that repo).
  * The reference is Mojo-internal (no FFI); its host code would bind these
- * symbols through `DLHandle` / `external_call` (see INTEGRATION.md).
+ * symbols through `DLHandle` / `external_call`.
  *
  * Conventions
  *   - Every function returns an int status (Q8_OK = 0).  On error the message
@@ -18,6 +18,13 @@
  *   - Model-level functions (q8_*) own all device memory of a context; host
  *     buffers passed to them belong to the caller.  A context is bound to one
  *     GPU and is not thread-safe.
+ *   - Per-device scratch (the decode GEMV's split-tile partials and tickets,
+ *     the tensor-core GEMM's split-K workspace and tickets, the op scratch) is
+ *     shared by every context and op-level call on a device.  Calls whose
+ *     kernels could overlap on the GPU (two contexts on one device driven from
+ *     different threads, op-level calls on several streams) must be
+ *     serialized by the caller.  Scratch that grows is never freed while the
+ *     process runs, so captured decode graphs keep valid pointers.
  *   - Packed Q8 weight rows keep the reference layout
  *     (qwen3_mojo/scripts/quantize.py:31-43, src/llama_q8.mojo:26-42):
  *     row of K inputs = [K/64 f16 scales | K int8 codes] = K/64 + K/2 uint16.
@@ -75,11 +82,20 @@ const char* q8_status_string(int status);
 /* Library build string (arch, version). */
 const char* q8_version(void);
 /* Synchronizes the current device, then reports and clears a timeout that a
-   bounded barrier wait inside a tensor-core GEMM recorded (Q8_ERR_TIMEOUT),
-   else Q8_OK.  The model entry points poll this themselves after a prefill;
-   op-level callers poll it when they synchronize.  No counterpart in the
+   bounded barrier wait inside a tensor-core GEMM or the decode attention
+   recorded (Q8_ERR_TIMEOUT), else Q8_OK.  The model entry points (q8_forward,
+   q8_forward_hidden, q8_decode, q8_generate) read both words after every call,
+   with the call's other results, and fail with Q8_ERR_TIMEOUT when one is set;
+   op-level callers poll this when they synchronize.  No counterpart in the
    reference (its kernels have no device-side waits). */
 int q8_device_status(void);
+/* Test aid (no counterpart in the reference): writes `value` into the device
+   error word of one kernel family on the current device, as a bounded wait
+   that gave up would (unit 0: tensor-core GEMM, unit 1: decode attention).
+   The next model call then reports Q8_ERR_TIMEOUT and clears the word; the
+   kernels themselves run unchanged unless a wait actually exceeds 2^20
+   cycles.  Synchronizes the device. */
+int q8_debug_set_device_status(int unit, int value);
 
 /* =================================================================== op level */
 

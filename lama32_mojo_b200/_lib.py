@@ -50,6 +50,7 @@ SIGNATURES = {
     "q8_status_string": [_I32],
     "q8_version": [],
     "q8_device_status": [],
+    "q8_debug_set_device_status": [_I32, _I32],
     "q8op_pack": [_P, _I64, _I64, _P, _P],
     "q8op_dequant": [_P, _I64, _I64, _P, _P],
     "q8op_gemm": [_P, _I32, _I64, _I64, _I64, _P, _I64, _P, _I64, _P],

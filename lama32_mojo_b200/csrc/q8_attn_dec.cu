@@ -602,6 +602,12 @@ int attention_decode_launch(const float* q, int64_t ldq, int T, const int32_t* p
   return ad_dispatch<false>(a, tm, hd, grid, st);
 }
 
+// Device address of this file's error word (per device, current device).
+int attn_dec_error_word(int** out) {
+  Q8_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(out), g_q8_device_error));
+  return Q8_OK;
+}
+
 int attn_dec_poll_error() {
   int v = 0;
   Q8_CUDA(cudaMemcpyFromSymbol(&v, g_q8_device_error, sizeof(int)));

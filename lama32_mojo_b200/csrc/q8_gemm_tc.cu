@@ -660,6 +660,11 @@ int tc_min_tokens() {
   return v;
 }
 
+int gemm_tc_error_word(int** out) {
+  Q8_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(out), g_q8_device_error));
+  return Q8_OK;
+}
+
 int gemm_tc_poll_error() {
   int v = 0;
   Q8_CUDA(cudaMemcpyFromSymbol(&v, g_q8_device_error, sizeof(int)));

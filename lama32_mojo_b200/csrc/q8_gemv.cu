@@ -809,7 +809,9 @@ int gemm_dispatch(int epi, const float* x32, int64_t ldx32, const __half* xs, in
   return gemv_launch(epi, x32, ldx32, xs, M, K, W, N, y, ldy, ys, st);
 }
 
-// Per-device scratch for the op-level entry points (XS copy of x).
+// Per-device scratch for the op-level entry points (XS copy of x).  Growing
+// it retires the old buffer instead of freeing it, so a graph that captured
+// an earlier op-level call keeps a valid pointer.
 struct OpScratch {
   void* ptr = nullptr;
   size_t bytes = 0;
@@ -821,7 +823,6 @@ int op_scratch(size_t bytes, void** out) {
   Q8_CUDA(cudaGetDevice(&dev));
   OpScratch& s = g_op_scratch[dev & 63];
   if (s.bytes < bytes) {
-    if (s.ptr) Q8_CUDA(cudaFree(s.ptr));
     s.ptr = nullptr;
     s.bytes = 0;
     if (cudaMalloc(&s.ptr, bytes) != cudaSuccess) {

@@ -531,6 +531,13 @@ bool gemv_d_supported(int M, int K, int N, bool rms, const void* W) {
 }
 
 // Scratch per device: split-tile partials and tickets (tickets zero at rest).
+// Growing it never frees the previous buffers: CUDA graphs captured earlier
+// (decode steps of any context on the device) keep their pointers, so the old
+// buffers stay allocated until the process exits.  The scratch is shared by
+// every context and op-level call on the device: launches that use it must
+// not run concurrently (the library's model calls run on one stream per
+// context; contexts on one device must not decode at the same time on
+// different streams).
 struct GdScratch {
   float* part = nullptr;
   int* ticket = nullptr;
@@ -545,9 +552,8 @@ static int gd_scratch(int tiles, float** part, int** ticket) {
   std::lock_guard<std::mutex> lk(g_gd_mu);
   GdScratch& s = g_gd[dev & 63];
   if (s.tiles < tiles) {
-    // grown only outside stream capture (the first calls of a shape run eagerly)
-    if (s.part) cudaFree(s.part);
-    if (s.ticket) cudaFree(s.ticket);
+    // grown only outside stream capture (the first calls of a shape run
+    // eagerly); the old buffers are retired, not freed
     s.part = nullptr;
     s.ticket = nullptr;
     s.tiles = 0;

@@ -43,6 +43,9 @@ int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int64_t x16lo, int 
                    float* y, int64_t ldy, __half* y16, int64_t ldy16, int64_t y16lo, cudaStream_t st);
 // After a synchronize: Q8_OK, or the timeout a pipeline wait recorded (cleared).
 int gemm_tc_poll_error();
+// Device address of the error word of the tensor-core GEMM file (read
+// asynchronously by the model calls together with their results).
+int gemm_tc_error_word(int** out);
 // Kernel attributes and the per-device split-K workspace (outside stream capture).
 int gemm_tc_prepare();
 // Smallest token batch the model runtime sends to the tensor-core GEMM.
@@ -94,6 +97,7 @@ size_t attention_decode_part_floats(int T, int nkv, int nsplit, int group, int h
 // context splits for `items` (token, kv head) pairs: about one CTA per SM
 int attention_decode_nsplit(int items, int maxlen);
 int attn_dec_poll_error();
+int attn_dec_error_word(int** out);
 // Fused RoPE / QK-norm / KV append for the decode attention: q and the new
 // k, v are read un-rotated from the q|k|v rows; kw / vw are the (same) pools.
 struct AttnRope {

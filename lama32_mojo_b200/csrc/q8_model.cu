@@ -177,6 +177,10 @@ struct q8_ctx {
   int tc_dmin = 16;        // decode batches from this size run the tensor-core pipeline
   ArState ar;             // one-shot P2P allreduce for decode (TP > 1)
   int* ar_status_pin = nullptr;
+  // error words of the files whose kernels have bounded waits (tensor-core
+  // GEMM, decode attention), copied after every call into dev_err_pin
+  int* dev_err[2] = {nullptr, nullptr};
+  int* dev_err_pin = nullptr;
   std::string err;
 
   uint8_t* warena = nullptr;
@@ -522,12 +526,25 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
 // The persistent decode step's status word: queued copy to pinned memory
 // with the call's other results, checked after the call's synchronize.
 static int mk_status_copy(q8_ctx* c) {
+  for (int i = 0; i < 2; ++i)
+    Q8_CUDA(cudaMemcpyAsync(c->dev_err_pin + i, c->dev_err[i], 4, cudaMemcpyDeviceToHost, c->st));
   if (c->mk) Q8_CUDA(cudaMemcpyAsync(c->mk_status_pin, c->mk_status, 4, cudaMemcpyDeviceToHost, c->st));
   if (c->ar.ok) Q8_CUDA(cudaMemcpyAsync(c->ar_status_pin, c->ar.status, 4, cudaMemcpyDeviceToHost, c->st));
   return Q8_OK;
 }
 
 static int mk_status_check(q8_ctx* c) {
+  if (c->dev_err_pin[0] != 0 || c->dev_err_pin[1] != 0) {
+    // a bounded wait gave up: the call's results are not trusted.  Clear the
+    // words so that later waits in those kernels run to their full bound.
+    const int v0 = c->dev_err_pin[0], v1 = c->dev_err_pin[1];
+    c->dev_err_pin[0] = c->dev_err_pin[1] = 0;
+    for (int i = 0; i < 2; ++i) Q8_CUDA(cudaMemsetAsync(c->dev_err[i], 0, 4, c->st));
+    Q8_CUDA(cudaStreamSynchronize(c->st));
+    set_error("%s: a bounded device wait timed out (device status %d)",
+              v0 ? "tensor-core GEMM" : "decode attention", v0 ? v0 : v1);
+    return Q8_ERR_TIMEOUT;
+  }
   if (c->ar.ok && *c->ar_status_pin != 0) {
     const int v = *c->ar_status_pin;
     *c->ar_status_pin = 0;
@@ -669,6 +686,7 @@ static int destroy_impl(q8_ctx* c) {
   for (void* p : ptrs)
     if (p) cudaFree(p);
   if (c->pin) cudaFreeHost(c->pin);
+  if (c->dev_err_pin) cudaFreeHost(c->dev_err_pin);
   if (c->mk_status_pin) cudaFreeHost(c->mk_status_pin);
   if (c->st) cudaStreamDestroy(c->st);
   delete c;
@@ -743,7 +761,7 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
     const char* e = getenv("Q8_TC");
     c->tc = C.hidden % 512 == 0 && c->qd % 512 == 0 && c->F % 512 == 0 && !(e && e[0] == '0');
     // Q8_TC_DECODE_MIN: decode batches from this many sequences use the
-    // tensor-core pipeline (default 32; the GEMV kernels below it)
+    // tensor-core pipeline (default 16; the GEMV kernels below it)
     const char* d = getenv("Q8_TC_DECODE_MIN");
     c->tc_dmin = d ? std::max(1, atoi(d)) : 16;
   }
@@ -878,6 +896,11 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
   }
   if (cudaMallocHost((void**)&c->pin, (size_t)T * 5 * 4) != cudaSuccess)
     return bail((set_error("cudaMallocHost failed"), Q8_ERR_OOM));
+  if (cudaMallocHost((void**)&c->dev_err_pin, 2 * 4) != cudaSuccess)
+    return bail((set_error("cudaMallocHost failed"), Q8_ERR_OOM));
+  c->dev_err_pin[0] = c->dev_err_pin[1] = 0;
+  if ((s = gemm_tc_error_word(&c->dev_err[0]))) return bail(s);
+  if ((s = attn_dec_error_word(&c->dev_err[1]))) return bail(s);
 
   if ((s = argmax_prepare())) return bail(s);
   // the tensor-core GEMM's kernel attributes and split-K workspace, before
@@ -1290,7 +1313,6 @@ static int forward_impl(q8_ctx* c, const int32_t* ids, int s, int seq, float* lo
     Q8_TRY(run_tokens(c, T, T > 1, nqb, c->qb_max, nsplit, T - 1, last ? 1 : 0, kv_read_bytes(c, lens)));
     // the pinned staging is rewritten next chunk: wait for the copies
     Q8_CUDA(cudaStreamSynchronize(c->st));
-    if (c->tc && T >= kTcMinTokens) Q8_TRY(gemm_tc_poll_error());
     c->n_cached[seq] += T;
     done += T;
   }
@@ -1340,8 +1362,9 @@ static int forward_hidden_impl(q8_ctx* c, const int32_t* ids, int s, int seq, in
     Q8_TRY(rmsnorm_launch(c->h, c->ypart, c->final_norm, T, c->H, c->cfg.eps, nullptr, nullptr, nullptr, c->st));
   }
   Q8_CUDA(cudaMemcpyAsync(out, c->h, (size_t)T * c->H * 4, cudaMemcpyDeviceToHost, c->st));
+  Q8_TRY(mk_status_copy(c));
   Q8_CUDA(cudaStreamSynchronize(c->st));
-  if (c->tc && T >= kTcMinTokens) Q8_TRY(gemm_tc_poll_error());
+  Q8_TRY(mk_status_check(c));
   return Q8_OK;
 }
 
@@ -1440,7 +1463,6 @@ static int decode_impl(q8_ctx* c, const int32_t* ids, const int32_t* seqs, int B
   Q8_TRY(mk_status_copy(c));
   Q8_CUDA(cudaStreamSynchronize(c->st));
   Q8_TRY(mk_status_check(c));
-  if (c->tc && B >= c->tc_dmin) Q8_TRY(gemm_tc_poll_error());
   for (int b = 0; b < B; ++b) c->n_cached[seqs[b]] += 1;
   return Q8_OK;
 }
@@ -1473,7 +1495,6 @@ static int generate_impl(q8_ctx* c, const int32_t* first, const int32_t* seqs, i
   Q8_TRY(mk_status_copy(c));
   Q8_CUDA(cudaStreamSynchronize(c->st));
   Q8_TRY(mk_status_check(c));
-  if (c->tc && B >= c->tc_dmin) Q8_TRY(gemm_tc_poll_error());
   for (int b = 0; b < B; ++b) c->n_cached[seqs[b]] += steps;
   return Q8_OK;
 }
@@ -1499,6 +1520,15 @@ int q8_set_n_cached(q8_ctx* ctx, int seq, int n) {
   Q8_CHECK_ARG(n >= 0 && n <= ctx->n_cached[seq], "q8_set_n_cached: can only shrink (have %d, asked %d)",
                ctx->n_cached[seq], n);
   ctx->n_cached[seq] = n;
+  return Q8_OK;
+}
+
+int q8_debug_set_device_status(int unit, int value) {
+  Q8_CHECK_ARG(unit == 0 || unit == 1, "q8_debug_set_device_status: unit must be 0 or 1");
+  int* w = nullptr;
+  Q8_TRY(unit == 0 ? gemm_tc_error_word(&w) : attn_dec_error_word(&w));
+  Q8_CUDA(cudaDeviceSynchronize());
+  Q8_CUDA(cudaMemcpy(w, &value, 4, cudaMemcpyHostToDevice));
   return Q8_OK;
 }
 

@@ -366,3 +366,31 @@ def test_batched_decode_matches_single_sequence_wide(cuda):
                 m.set_n_cached(n0[b], b)
     finally:
         m.close()
+
+
+@pytest.mark.parametrize("unit", [1, 0])
+def test_device_wait_timeout_fails_the_call(cuda, unit):
+    """A bounded device wait that gave up leaves its code in its file's error
+    word (unit 1: decode attention, unit 0: tensor-core GEMM).  The model
+    calls read both words with their results: the call fails with
+    Q8_ERR_TIMEOUT, the word is cleared, and the next call succeeds with the
+    oracle's token.  The word is set from the host, so no wait is made to time
+    out on the GPU."""
+    from lama32_mojo_b200._lib import Q8_ERR_TIMEOUT, lib
+    cfgname = "tiny-llama"
+    ocfg = O.PRESETS[cfgname]
+    orc = O.OracleModel(ocfg, O.make_q8_checkpoint(ocfg))
+    ids = O.random_ids(ocfg, 9, seed=21)
+    t0 = orc.forward_argmax(ids)
+    t1 = orc.forward_argmax([t0])
+    m = build(cfgname, maxlen=32)
+    assert m.forward_argmax(ids) == t0
+    assert lib().q8_debug_set_device_status(unit, Q8_ERR_TIMEOUT) == 0
+    with pytest.raises(Q8Error) as e:
+        m.decode([t0], [0])
+    assert e.value.status == Q8_ERR_TIMEOUT
+    assert m.n_cached == len(ids)  # the failed step did not advance the cache
+    assert int(m.decode([t0], [0])[0]) == t1
+    assert m.n_cached == len(ids) + 1
+    assert lib().q8_device_status() == 0
+    m.close()
