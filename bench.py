@@ -270,18 +270,17 @@ def main():
             s[1] += kb
             s[2] += kl
     m.set_profiling(False)
-    # dominant kernel: the persistent decode step when it runs (one launch per
-    # step, all GEMVs + attention), else the Q8 GEMV launches of the step
+    # dominant kernel: the one-launch weight-ring decode step when it runs
+    # (every GEMV, attention and norm of a step), else the Q8 GEMV launches
     dom = ["decode_step"] if "decode_step" in agg else [k for k in agg if k.startswith("gemv_")]
-    dom_name = ("k_decode_step (persistent decode step: every GEMV, attention and norm of one step)"
-                if dom == ["decode_step"] else "k_gemv_q8 (all Q8 GEMV launches of a decode step)")
+    dom_name = ("k_decode_ring (one-launch decode step: weights + KV of the whole step)"
+                if dom == ["decode_step"] else "k_gemv_d (all Q8 GEMV launches of a decode step)")
     g_ms = sum(agg[k][0] for k in dom)
     g_b = sum(agg[k][1] for k in dom)
     g_l = sum(agg[k][2] for k in dom)
     peak, peak_kind = load_peaks()
     achieved = g_b / (g_ms / 1e3) / 1e9 if g_ms > 0 else 0.0
-    # "phase:*" entries split the persistent step's time (no launches of their own)
-    step_ms_prof = sum(v[0] for k, v in agg.items() if not k.startswith(("phase:", "sub:"))) / nprof
+    step_ms_prof = sum(v[0] for v in agg.values()) / nprof
     breakdown = {k: {"ms_per_step": round(v[0] / nprof, 4), "launches_per_step": v[2] // nprof,
                      "GB_s": round(v[1] / (v[0] / 1e3) / 1e9, 1) if v[0] > 0 else None} for k, v in agg.items()}
     traffic = None

@@ -1,0 +1,1065 @@
+// Weight-ring decode step: one cooperative launch runs a whole decode step
+// of one sequence (embed -> L x [RMSNorm, q|k|v, QK-norm + RoPE + KV append,
+// GQA attention, o_proj + residual, RMSNorm, gate|up + SwiGLU, down +
+// residual] -> final RMSNorm -> lm_head -> greedy argmax).
+//
+// Replaces, for batch-1 decode, the per-op dispatch chain of run_layer_q8
+// (src/llama_q8.mojo:144-230) and the model shell's forward_argmax
+// (qwen3_mojo/src/qwen_q8.mojo:126-162, src/llama_gpu.mojo:119-155), with
+// the arithmetic of k_mm_q8 (src/llama_q8.mojo:54-93), k_rmsnorm_w / k_res_add
+// (src/llama_common.mojo:197-225, :354-358), k_rmsnorm2_w (:228-270),
+// k_rope_qk_copy2 (:299-342), k_scores / k_softmax_rows / k_att_out
+// (:402-473), k_swiglu_mul (:476-481) and k_argmax (:493-519).
+//
+// Why one launch with a ring.  At batch 1 a decode step is a chain of ~160
+// dependent operations over 7.7 GB of weights (Llama-3.1-8B); with one kernel
+// per operation every boundary drains the memory pipeline (launch, ramp,
+// activation staging, tail: ~11 us each).  Weight bytes never depend on the
+// activations, so here one CTA per SM splits into
+//   * a producer warp that walks the CTA's share of every phase of the step
+//     in order (its tiles of each matrix, its KV blocks of each layer's
+//     attention) and streams them with bulk copies (TMA engine) into a ring
+//     of shared-memory slots, waiting only for free slots, and
+//   * 8 consumer warps that wait for the previous phase of the whole grid
+//     (a monotonic arrival counter), stage the phase's activation vector once
+//     per CTA, and drain the ring.
+// The producer therefore runs up to a ring's worth of bytes (136 KB per SM)
+// ahead across phase and layer boundaries, and HBM keeps streaming while the
+// grid synchronizes.
+//
+// Ring.  Consumer warp w owns slots 2w and 2w+1 (full / empty mbarrier pair
+// each) and takes its items in order, alternating slots; the producer fills
+// them in the same order, so no wait ever targets a phase more than one
+// ahead.  A GEMV stage is 16 weight rows x 512 codes (rows padded to 528 B in
+// shared memory so that ldmatrix is conflict-free) plus their 16 x 8 f16
+// group scales; an attention block is 16 K rows (padded) in one slot and 16
+// V rows in the other.
+//
+// GEMV arithmetic (as the standalone digit GEMV): int8 codes straight to
+// mma.m16n8k32.s8 against the activations written as three int8 digits per
+// value with one f32 scale per 64-group, x ~ e (a0 + a1/254 + a2/254^2), so
+// the exact integer dot products carry the f32 activations; per group and
+// digit column the s32 sum is scaled by (f16 weight scale) x (e / 254^d).
+//
+// Work split.  A matrix of T 16-row tiles (SwiGLU: 8 gate + 8 up rows) and C
+// = K/512 chunks has T*C stages.  q|k|v, o_proj, gate|up and lm_head give
+// each CTA whole tiles (so their epilogues finish rows: store, residual add,
+// SwiGLU, logits + argmax); down_proj, whose tiles are 14336 codes deep,
+// gives each CTA an even share of stages and parks partial rows in per-CTA
+// slots that the next phase's staging adds to the residual in slot order.
+// A CTA's stages are cut into 8 contiguous runs, one per consumer warp; a
+// warp's per-tile sums go to shared memory and are added in warp order.
+// The residual alternates between two buffers by layer, so a staging that
+// folds the down partials into the residual never races with another CTA
+// reading the old value.  Attention: CTA (kv head, context split), 16-
+// position blocks, online softmax; the last split CTA of a kv head (release /
+// acquire ticket) merges the splits in order.  Every sum has a fixed order:
+// results do not depend on timing.
+//
+// Every wait is bounded (about a second): a wait that gives up sets the
+// device status word, after which every other wait returns at once and the
+// host reports Q8_ERR_TIMEOUT.  No load uses cluster multicast.
+#include "q8_decode_ring.h"
+#include "q8_kernels.h"
+
+#include <algorithm>
+#include <mutex>
+
+namespace q8 {
+
+enum { DP_QKV = 0, DP_ATTN = 1, DP_O = 2, DP_GU = 3, DP_DOWN = 4, DP_LM = 5 };
+
+constexpr int DR_RING = DR_SLOTS * DR_SLOT_BYTES;
+constexpr int DR_FCOL_BYTES = 256 * 16;  // K <= 16384
+constexpr int DR_ATT_BYTES = (DR_GMAX * 128 + DR_CW * DR_GMAX * 16 + 2 * 128) * 4;
+constexpr int DR_SMEM = 1024 + DR_RING + DR_XQ_BYTES + DR_FCOL_BYTES + DR_ATT_BYTES + 2 * DR_SLOTS * 8;
+
+// ------------------------------------------------------------------ small helpers
+__device__ __forceinline__ unsigned int dr_ld_acquire(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ int dr_ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+
+// barrier 1 over the 8 consumer warps (the producer never joins)
+__device__ __forceinline__ void dr_csync() { asm volatile("bar.sync 1, %0;" ::"n"(DR_CW * 32) : "memory"); }
+
+__device__ __forceinline__ void dr_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Bounded mbarrier wait: gives up after ~2^31 cycles (setting the status
+// word) or as soon as another wait has given up (checked every 2^10 polls).
+__device__ __forceinline__ bool dr_mwait(uint64_t* bar, uint32_t parity, int* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (unsigned it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 0x3FFu) == 0) {
+      if (dr_ld_volatile(status)) return false;
+      if (clock64() - t0 > (1ll << 31)) {
+        atomicExch(status, Q8_ERR_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+// Grid phase barrier (consumer warps only): wait until every CTA has arrived
+// `target` times in total, then release the CTA's consumers.
+__device__ __forceinline__ void dr_grid_wait(const DrParams& P, unsigned int target) {
+  if (threadIdx.x == 0 && dr_ld_volatile(P.status) == 0) {
+    const long long t0 = clock64();
+    for (unsigned it = 1; dr_ld_acquire(P.bar) < target; ++it) {
+      if ((it & 63u) == 0) {
+        if (dr_ld_volatile(P.status)) break;
+        if (clock64() - t0 > (1ll << 31)) {
+          atomicExch(P.status, Q8_ERR_TIMEOUT);
+          break;
+        }
+      }
+    }
+  }
+  dr_csync();
+}
+
+// Every consumer thread's stores of the phase, then one gpu-scope release.
+__device__ __forceinline__ void dr_grid_arrive(const DrParams& P) {
+  dr_csync();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(P.bar, 1u);
+  }
+}
+
+__device__ __forceinline__ void dr_ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void dr_imma(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ------------------------------------------------------------------ phases
+// Phase ph of the step: layer ph / 5, kind ph % 5; the last phase is lm_head.
+__device__ __forceinline__ int dr_kind(const DrParams& P, int ph) { return ph == 5 * P.L ? DP_LM : ph % 5; }
+
+// One GEMV phase as one CTA sees it.
+struct DrG {
+  const uint8_t* W;
+  int64_t rb;
+  int K, C, T;   // inputs, 512-code chunks per row, 16-row tiles
+  int F2;        // SwiGLU: rows of tile t are gate t*8.. and up F2 + t*8..; 0: rows t*16..
+  int s0, s1;    // this CTA's stages [s0, s1) of T*C
+  int split;     // tiles may be shared by CTAs (partial rows into slots)
+};
+
+__device__ __forceinline__ DrG dr_gemv_desc(const DrParams& P, int kind, int L) {
+  DrG d;
+  int N;
+  const DrLayer* ly = P.layers + (kind == DP_LM ? 0 : L);
+  d.F2 = 0;
+  d.split = 0;
+  switch (kind) {
+    case DP_QKV: d.W = ly->qkv; d.K = P.H; N = P.nqkv; break;
+    case DP_O: d.W = ly->o; d.K = P.qd; N = P.H; break;
+    case DP_GU: d.W = ly->gu; d.K = P.H; N = P.F; d.F2 = P.F; break;
+    case DP_DOWN: d.W = ly->down; d.K = P.F; N = P.H; d.split = 1; break;
+    default: d.W = P.lm_head; d.K = P.H; N = P.V; break;
+  }
+  d.T = d.F2 ? N / 8 : N / 16;
+  d.C = d.K / DR_CK;
+  d.rb = (int64_t)d.K + d.K / 32;
+  const int G = gridDim.x, c = blockIdx.x;
+  if (d.split) {  // over the first min(G, S) CTAs, so that every range holds a stage
+    const long long S = (long long)d.T * d.C;
+    const int Gs = (int)min((long long)G, S);
+    d.s0 = c < Gs ? (int)(S * c / Gs) : (int)S;
+    d.s1 = c < Gs ? (int)(S * (c + 1) / Gs) : (int)S;
+  } else {
+    d.s0 = (int)((long long)d.T * c / G) * d.C;
+    d.s1 = (int)((long long)d.T * (c + 1) / G) * d.C;
+  }
+  return d;
+}
+
+// CTA whose split range holds stage x: the largest c with floor(c S / Gs) <=
+// x, Gs = min(G, S) (every one of those ranges is non-empty).
+__device__ __forceinline__ int dr_cta_of(long long x, long long S) {
+  const long long Gs = min((long long)gridDim.x, S);
+  return (int)(((x + 1) * Gs - 1) / S);
+}
+
+// Partial slots of down-projection tile t (rows t*16 .. t*16+15): one per
+// CTA whose range meets the tile, in CTA order.
+__device__ __forceinline__ int dr_down_slots(const DrParams& P, int t) {
+  const int C = P.F / DR_CK;
+  const long long S = (long long)(P.H / 16) * C;
+  return dr_cta_of((long long)(t + 1) * C - 1, S) - dr_cta_of((long long)t * C, S) + 1;
+}
+
+// ------------------------------------------------------------------ producer
+__device__ __forceinline__ void dr_issue_stage(const DrParams& P, const DrG& d, int st, uint8_t* ring, uint64_t* full,
+                                               uint64_t* empty, int slot, int use, int lane) {
+  if (use > 0) dr_mwait(&empty[slot], (uint32_t)((use - 1) & 1), P.status);
+  uint8_t* dst = ring + slot * DR_SLOT_BYTES;
+  const int t = st / d.C, ch = st % d.C;
+  if (lane == 0) mbar_arrive_expect_tx(&full[slot], 16 * DR_CK + 16 * 16);
+  __syncwarp();
+  const int r = lane & 15;
+  const int64_t row = d.F2 ? (r < 8 ? (int64_t)t * 8 + r : (int64_t)d.F2 + (int64_t)t * 8 + (r - 8))
+                           : (int64_t)t * 16 + r;
+  const uint8_t* src = d.W + row * d.rb;
+  if (lane < 16) bulk_g2s(dst + r * DR_RS, src + d.K / 32 + (int64_t)ch * DR_CK, DR_CK, &full[slot]);
+  else bulk_g2s(dst + 16 * DR_RS + r * 16, src + (int64_t)ch * 16, 16, &full[slot]);
+}
+
+template <int HD>
+__device__ __forceinline__ void dr_produce_attn(const DrParams& P, int L, uint8_t* ring, uint64_t* full,
+                                                uint64_t* empty, int (&u)[DR_CW], int lane) {
+  const int c = blockIdx.x, ns = P.nsplit;
+  if (c >= P.nkv * ns) return;
+  const int kvh = c / ns, sp = c % ns;
+  const int p = P.pos[0], kv_end = p + 1, nb = (kv_end + 15) / 16;
+  const int bl0 = (int)((long long)sp * nb / ns), bl1 = (int)((long long)(sp + 1) * nb / ns);
+  const int32_t* btr = P.bt + (int64_t)P.seq[0] * P.max_pages;
+  const float* kp = P.layers[L].kp;
+  const float* vp = P.layers[L].vp;
+  const int nblk = bl1 - bl0;
+  for (int r = 0; r * DR_CW < nblk; ++r) {
+#pragma unroll
+    for (int w = 0; w < DR_CW; ++w) {
+      const int i = r * DR_CW + w;
+      if (i < nblk) {
+        const int sk = 2 * w + (u[w] & 1), uk = u[w] >> 1;
+        const int sv = 2 * w + ((u[w] + 1) & 1), uv = (u[w] + 1) >> 1;
+        if (uk > 0) dr_mwait(&empty[sk], (uint32_t)((uk - 1) & 1), P.status);
+        if (uv > 0) dr_mwait(&empty[sv], (uint32_t)((uv - 1) & 1), P.status);
+        const int key0 = (bl0 + i) * 16;
+        const int64_t row0 = ((int64_t)btr[key0 / P.page] * P.nkv + kvh) * P.page + (key0 % P.page);
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[sk], 16 * HD * 4);
+          mbar_arrive_expect_tx(&full[sv], 16 * HD * 4);
+        }
+        __syncwarp();
+        if (lane < 16)
+          bulk_g2s(ring + sk * DR_SLOT_BYTES + lane * (HD * 4 + 16), kp + (row0 + lane) * HD, HD * 4, &full[sk]);
+        else if (lane == 16)
+          bulk_g2s(ring + sv * DR_SLOT_BYTES, vp + row0 * HD, 16 * HD * 4, &full[sv]);
+        u[w] += 2;
+      }
+    }
+  }
+}
+
+template <int HD>
+__device__ void dr_producer(const DrParams& P, uint8_t* ring, uint64_t* full, uint64_t* empty) {
+  const int lane = threadIdx.x & 31;
+  int u[DR_CW];
+#pragma unroll
+  for (int w = 0; w < DR_CW; ++w) u[w] = 0;
+  const int nphase = 5 * P.L + 1;
+  for (int ph = 0; ph < nphase; ++ph) {
+    if (dr_ld_volatile(P.status)) break;
+    const int kind = dr_kind(P, ph), L = ph / 5;
+    if (kind == DP_ATTN) {
+      dr_produce_attn<HD>(P, L, ring, full, empty, u, lane);
+      continue;
+    }
+    const DrG d = dr_gemv_desc(P, kind, L);
+    const int n = d.s1 - d.s0, runs = (n + DR_CW - 1) / DR_CW;
+    for (int r = 0; r < runs; ++r) {
+#pragma unroll
+      for (int w = 0; w < DR_CW; ++w) {
+        const int a = d.s0 + (int)((long long)n * w / DR_CW), b = d.s0 + (int)((long long)n * (w + 1) / DR_CW);
+        if (a + r < b) {
+          dr_issue_stage(P, d, a + r, ring, full, empty, 2 * w + (u[w] & 1), u[w] >> 1, lane);
+          ++u[w];
+        }
+      }
+    }
+  }
+  // no copy may still be landing in this CTA's shared memory when it exits
+#pragma unroll
+  for (int w = 0; w < DR_CW; ++w) {
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      const int uses = (u[w] + 1 - b) >> 1;
+      if (uses > 0) dr_mwait(&full[2 * w + b], (uint32_t)((uses - 1) & 1), P.status);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ activation staging
+// Digits of one 64-group into xq [group][digit][64] with the k order the
+// B fragments read (byte t*16 + j*4 + b holds k = 16 j + 4 t + b, so lane t
+// of a quad gets both k32 halves of the group with one 16-byte load), and
+// (e, e/254, e/254^2, 0) into fcol [group].  Four lanes per group (sq = lane &
+// 3 holds k = 16 sq .. 16 sq + 15); every lane of the warp takes part.
+__device__ __forceinline__ void dr_digits16(const float (&v)[16], bool valid, int gi, int sq, uint8_t* xq,
+                                            float4* fcol) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  if (!valid) return;
+  const float e = amax / 127.0f;
+  const float ie = amax > 0.f ? 127.0f / amax : 0.f;
+  uint32_t w[3][4];
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    uint32_t p0 = 0, p1 = 0, p2 = 0;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      float x = v[4 * t + b] * ie;
+      const int d0 = max(-127, min(127, __float2int_rn(x)));
+      x = (x - (float)d0) * 254.0f;
+      const int d1 = max(-127, min(127, __float2int_rn(x)));
+      x = (x - (float)d1) * 254.0f;
+      const int d2 = max(-127, min(127, __float2int_rn(x)));
+      p0 |= (uint32_t)(d0 & 0xFF) << (8 * b);
+      p1 |= (uint32_t)(d1 & 0xFF) << (8 * b);
+      p2 |= (uint32_t)(d2 & 0xFF) << (8 * b);
+    }
+    w[0][t] = p0;
+    w[1][t] = p1;
+    w[2][t] = p2;
+  }
+  uint8_t* dq = xq + (int64_t)gi * 192 + sq * 4;
+#pragma unroll
+  for (int dg = 0; dg < 3; ++dg)
+#pragma unroll
+    for (int t = 0; t < 4; ++t) *reinterpret_cast<uint32_t*>(dq + dg * 64 + t * 16) = w[dg][t];
+  if (sq == 0) fcol[gi] = make_float4(e, e / 254.0f, e / 64516.0f, 0.f);
+}
+
+enum { DS_F32 = 0, DS_EMBED = 1, DS_FOLD = 2 };
+
+// 16 values x[k0 .. k0+15] of the phase's input vector.
+__device__ __forceinline__ void dr_load16(const DrParams& P, int kind, const float* src, int k0, float (&v)[16]) {
+  if (kind == DS_EMBED) {
+    const int64_t rb = (int64_t)P.H + P.H / 32;
+    const uint8_t* row = P.embed + (int64_t)P.ids[0] * rb;
+    const float s = __half2float(__ushort_as_half(reinterpret_cast<const unsigned short*>(row)[k0 / 64]));
+    const uint4 q = *reinterpret_cast<const uint4*>(row + P.H / 32 + k0);
+    const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = (float)(int8_t)((qw[i >> 2] >> (8 * (i & 3))) & 0xFF) * s;
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(src + k0) + i);
+    v[4 * i] = a.x; v[4 * i + 1] = a.y; v[4 * i + 2] = a.z; v[4 * i + 3] = a.w;
+  }
+  if (kind == DS_FOLD) {  // residual + the down partial slots of its tile, in slot order
+    const int ns = dr_down_slots(P, k0 / 16);
+    for (int s = 0; s < ns; ++s) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 a = __ldcg(reinterpret_cast<const float4*>(P.pres + (int64_t)s * P.H + k0) + i);
+        v[4 * i] += a.x; v[4 * i + 1] += a.y; v[4 * i + 2] += a.z; v[4 * i + 3] += a.w;
+      }
+    }
+  }
+}
+
+// Stages the K inputs of a GEMV phase as digits: x from `kind`; with nw,
+// x = nw * x / sqrt(mean(x^2) + eps) (K <= 8192); with wb, this CTA's slice
+// of the raw x is written back (the residual of the layer).
+__device__ void dr_stage(const DrParams& P, int K, int kind, const float* src, const uint16_t* nw, float* wb,
+                         uint8_t* xq, float4* fcol, float* scr) {
+  constexpr int NT = DR_CW * 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, sq = lane & 3;
+  const int nitem = K / 16;  // quarter-groups
+  if (nw) {
+    float v[2][16];
+    float ss = 0.f;
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+      const int item = it * NT + tid;
+      if (item < nitem) {
+        const int k0 = item * 16;
+        dr_load16(P, kind, src, k0, v[it]);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) ss = fmaf(v[it][i], v[it][i], ss);
+        if (wb) {
+          const int G = gridDim.x, c = blockIdx.x;
+          const int w0 = (int)((long long)K * c / G), w1 = (int)((long long)K * (c + 1) / G);
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (k0 + i >= w0 && k0 + i < w1) wb[k0 + i] = v[it][i];
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[it][i] = 0.f;
+      }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) scr[warp] = ss;
+    dr_csync();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < DR_CW; ++w) tot += scr[w];
+    const float inv = 1.0f / sqrtf(tot / (float)K + P.eps);
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+      const int item = it * NT + tid;
+      const bool valid = item < nitem;
+      if (valid) {
+        const int k0 = item * 16;
+        const uint4 w0 = __ldg(reinterpret_cast<const uint4*>(nw + k0));
+        const uint4 w1 = __ldg(reinterpret_cast<const uint4*>(nw + k0 + 8));
+        const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          v[it][2 * i] = __uint_as_float(ww[i] << 16) * v[it][2 * i] * inv;
+          v[it][2 * i + 1] = __uint_as_float(ww[i] & 0xFFFF0000u) * v[it][2 * i + 1] * inv;
+        }
+      }
+      if (it * NT < nitem) dr_digits16(v[it], valid, valid ? item >> 2 : 0, sq, xq, fcol);
+    }
+  } else {
+    for (int base = 0; base < nitem; base += NT) {
+      float v[16];
+      const int item = base + tid;
+      const bool valid = item < nitem;
+      if (valid) {
+        dr_load16(P, kind, src, item * 16, v);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = 0.f;
+      }
+      dr_digits16(v, valid, valid ? item >> 2 : 0, sq, xq, fcol);
+    }
+  }
+  dr_csync();
+}
+
+// ------------------------------------------------------------------ GEMV consumer
+// A warp's sums of local tile lt: row g = digit columns 0 + 1 (lane t = 0)
+// + 2 (lane t = 1), in column order; the same for row g + 8.
+__device__ __forceinline__ void dr_flush(float* red, int lt, int warp, int g, int t, const float (&acc)[4]) {
+  const float x0 = __shfl_sync(0xffffffffu, acc[0], g * 4 + 1);
+  const float x2 = __shfl_sync(0xffffffffu, acc[2], g * 4 + 1);
+  if (t == 0) {
+    float* rw = red + (lt * DR_CW + warp) * 16;
+    rw[g] = acc[0] + acc[1] + x0;
+    rw[g + 8] = acc[2] + acc[3] + x2;
+  }
+}
+
+// Warp `warp` drains its run of the CTA's stages; per-tile sums into red
+// [local tile][warp][16 rows].
+__device__ __forceinline__ void dr_gemv_run(const DrParams& P, const DrG& d, uint8_t* ring, uint64_t* full,
+                                            uint64_t* empty, const uint8_t* xq, const float4* fcol, float* red,
+                                            int& u, int warp, int lane) {
+  const int n = d.s1 - d.s0;
+  const int a = d.s0 + (int)((long long)n * warp / DR_CW), b = d.s0 + (int)((long long)n * (warp + 1) / DR_CW);
+  const int t_lo = d.s0 / d.C;
+  const int g = lane >> 2, t = lane & 3;
+  const int mat = lane >> 3, rr = lane & 7;
+  const uint32_t lofs = (uint32_t)((rr + 8 * (mat & 1)) * DR_RS + 16 * (mat >> 1));
+  const bool has_col = g < 3;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  int cur = -1;
+  for (int st = a; st < b; ++st) {
+    const int tile = st / d.C, ch = st % d.C;
+    if (tile != cur) {
+      if (cur >= 0) dr_flush(red, cur - t_lo, warp, g, t, acc);
+      cur = tile;
+      acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+    }
+    const int slot = 2 * warp + (u & 1);
+    dr_mwait(&full[slot], (uint32_t)((u >> 1) & 1), P.status);
+    const uint8_t* sb = ring + slot * DR_SLOT_BYTES;
+    const uint32_t sbase = smem_u32(sb) + lofs;
+    const uint4 sA = *reinterpret_cast<const uint4*>(sb + 16 * DR_RS + g * 16);
+    const uint4 sB = *reinterpret_cast<const uint4*>(sb + 16 * DR_RS + (g + 8) * 16);
+#pragma unroll
+    for (int grp = 0; grp < 8; ++grp) {
+      const int gi = ch * 8 + grp;
+      uint32_t a0, a1, a2, a3, a4, a5, a6, a7;
+      dr_ldsm_x4(sbase + grp * 64, a0, a1, a2, a3);
+      dr_ldsm_x4(sbase + grp * 64 + 32, a4, a5, a6, a7);
+      uint4 bx = make_uint4(0, 0, 0, 0);
+      if (has_col) bx = *reinterpret_cast<const uint4*>(xq + (int64_t)gi * 192 + g * 64 + t * 16);
+      int dd[4] = {0, 0, 0, 0};
+      dr_imma(dd, a0, a1, a2, a3, bx.x, bx.y);
+      dr_imma(dd, a4, a5, a6, a7, bx.z, bx.w);
+      const float4 f = fcol[gi];
+      const float fc0 = t == 0 ? f.x : (t == 1 ? f.z : 0.f);
+      const float fc1 = t == 0 ? f.y : 0.f;
+      const uint32_t wa = (grp >> 1) == 0 ? sA.x : ((grp >> 1) == 1 ? sA.y : ((grp >> 1) == 2 ? sA.z : sA.w));
+      const uint32_t wb = (grp >> 1) == 0 ? sB.x : ((grp >> 1) == 1 ? sB.y : ((grp >> 1) == 2 ? sB.z : sB.w));
+      const float sa = __half2float(__ushort_as_half((unsigned short)((grp & 1) ? (wa >> 16) : (wa & 0xFFFFu))));
+      const float sc = __half2float(__ushort_as_half((unsigned short)((grp & 1) ? (wb >> 16) : (wb & 0xFFFFu))));
+      acc[0] = fmaf(__int2float_rn(dd[0]), sa * fc0, acc[0]);
+      acc[1] = fmaf(__int2float_rn(dd[1]), sa * fc1, acc[1]);
+      acc[2] = fmaf(__int2float_rn(dd[2]), sc * fc0, acc[2]);
+      acc[3] = fmaf(__int2float_rn(dd[3]), sc * fc1, acc[3]);
+    }
+    __syncwarp();
+    if (lane == 0) dr_arrive(&empty[slot]);
+    ++u;
+  }
+  if (cur >= 0) dr_flush(red, cur - t_lo, warp, g, t, acc);
+}
+
+// Sum of row r (0..15) of local tile lt over the warps whose runs cover it.
+__device__ __forceinline__ float dr_tile_sum(const DrG& d, const float* red, int lt, int r) {
+  const int n = d.s1 - d.s0, tile = d.s0 / d.C + lt;
+  const int ta = max(d.s0, tile * d.C), tb = min(d.s1, (tile + 1) * d.C);
+  float v = 0.f;
+#pragma unroll
+  for (int w = 0; w < DR_CW; ++w) {
+    const int a = d.s0 + (int)((long long)n * w / DR_CW), b = d.s0 + (int)((long long)n * (w + 1) / DR_CW);
+    if (a < b && a < tb && b > ta) v += red[(lt * DR_CW + w) * 16 + r];
+  }
+  return v;
+}
+
+__device__ __forceinline__ unsigned long long dr_key(float v, int idx) {
+  uint32_t b = __float_as_uint(v);
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)b << 32) | (uint32_t)(~(uint32_t)idx);
+}
+
+// ------------------------------------------------------------------ attention consumer
+template <int HD>
+__device__ void dr_attn(const DrParams& P, int L, uint8_t* ring, uint64_t* full, uint64_t* empty, int& u, float* sQ,
+                        float* sP, float* sKn, float* sVn, float* sX, float (*sm_m)[DR_GMAX],
+                        float (*sm_l)[DR_GMAX], int* s_last) {
+  constexpr int E = HD / 32, CH = HD / 4, J = HD / 32, KR = HD + 4;
+  const int c = blockIdx.x, ns = P.nsplit;
+  if (c >= P.nkv * ns) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kvh = c / ns, sp = c % ns, G = P.nh / P.nkv;
+  const int p = P.pos[0], kv_end = p + 1, nb = (kv_end + 15) / 16;
+  const int bl0 = (int)((long long)sp * nb / ns), bl1 = (int)((long long)(sp + 1) * nb / ns);
+  const int nblk = bl1 - bl0;
+  const int32_t* btr = P.bt + (int64_t)P.seq[0] * P.max_pages;
+  const DrLayer* ly = P.layers + L;
+  const bool own_new = p >= bl0 * 16 && p < bl1 * 16;
+
+  // prologue: the G q heads (QK-norm, RoPE, scaled) into sQ; the split that
+  // holds position p rotates the new k, appends k and v to the cache and keeps
+  // them in sKn / sVn for its own block
+  {
+    const float qscale = 1.4426950408889634f / sqrtf((float)HD);
+    const int ntask = G + (own_new ? 1 : 0);
+    const int tsk = warp;  // one task per warp (G + 1 <= DR_CW)
+    if (tsk < ntask) {
+      float v[J], vv[J];
+      const float* src = P.qkv + (tsk < G ? (int64_t)(kvh * G + tsk) * HD : (int64_t)(P.nh + kvh) * HD);
+#pragma unroll
+      for (int j = 0; j < J; ++j) v[j] = __ldcg(src + lane + 32 * j);
+      if (tsk == G) {
+        const float* vsrc = P.qkv + (int64_t)(P.nh + P.nkv + kvh) * HD;
+#pragma unroll
+        for (int j = 0; j < J; ++j) vv[j] = __ldcg(vsrc + lane + 32 * j);
+      }
+      const uint16_t* nw = tsk < G ? ly->q_norm : ly->k_norm;
+      if (nw) {
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < J; ++j) ss = fmaf(v[j], v[j], ss);
+        ss = warp_sum(ss);
+        const float inv = 1.0f / sqrtf(ss / (float)HD + P.eps);
+#pragma unroll
+        for (int j = 0; j < J; ++j) v[j] = bf16_bits_to_f32(nw[lane + 32 * j]) * v[j] * inv;
+      }
+      const float fp = (float)p;
+#pragma unroll
+      for (int j = 0; j < J / 2; ++j) {
+        float sn, cs;
+        sincosf(fp * P.inv_freq[lane + 32 * j], &sn, &cs);
+        const float x0 = v[j], x1 = v[j + J / 2];
+        v[j] = x0 * cs - x1 * sn;
+        v[j + J / 2] = x1 * cs + x0 * sn;
+      }
+      if (tsk < G) {
+#pragma unroll
+        for (int j = 0; j < J; ++j) sQ[tsk * HD + lane + 32 * j] = v[j] * qscale;
+      } else {
+        const int64_t off = (((int64_t)btr[p / P.page] * P.nkv + kvh) * P.page + (p % P.page)) * HD;
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+          ly->kp[off + lane + 32 * j] = v[j];
+          ly->vp[off + lane + 32 * j] = vv[j];
+          sKn[lane + 32 * j] = v[j];
+          sVn[lane + 32 * j] = vv[j];
+        }
+      }
+    }
+    dr_csync();
+  }
+
+  float m[DR_GMAX], l[DR_GMAX], o[DR_GMAX][E];
+#pragma unroll
+  for (int g = 0; g < DR_GMAX; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) o[g][e] = 0.f;
+  }
+  float* pw = sP + warp * DR_GMAX * 16;
+  const int jr = lane >> 1, hh = 4 * (lane & 1);
+  const bool lead = (lane & 1) == 0;
+  for (int i = warp; i < nblk; i += DR_CW) {
+    const int sk = 2 * warp + (u & 1), uk = u >> 1;
+    const int sv = 2 * warp + ((u + 1) & 1), uv = (u + 1) >> 1;
+    const int key0 = (bl0 + i) * 16;
+    const int nv = min(16, kv_end - key0);
+    float* kb = reinterpret_cast<float*>(ring + sk * DR_SLOT_BYTES);
+    float* vb = reinterpret_cast<float*>(ring + sv * DR_SLOT_BYTES);
+    dr_mwait(&full[sk], (uint32_t)(uk & 1), P.status);
+    dr_mwait(&full[sv], (uint32_t)(uv & 1), P.status);
+    if (own_new && p >= key0 && p < key0 + 16) {  // the appended row, from the prologue
+      for (int c4 = lane; c4 < CH; c4 += 32) {
+        *reinterpret_cast<float4*>(kb + (p - key0) * KR + 4 * c4) = *reinterpret_cast<const float4*>(sKn + 4 * c4);
+        *reinterpret_cast<float4*>(vb + (p - key0) * HD + 4 * c4) = *reinterpret_cast<const float4*>(sVn + 4 * c4);
+      }
+      // these generic writes land before the bulk copy that later refills the slots
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+    }
+    float s[DR_GMAX];
+    {
+      float s0[DR_GMAX], s1[DR_GMAX];
+#pragma unroll
+      for (int g = 0; g < DR_GMAX; ++g) s0[g] = s1[g] = 0.f;
+      const float4* q4 = reinterpret_cast<const float4*>(sQ);
+#pragma unroll 2
+      for (int cc = 0; cc < CH / 2; cc += 2) {
+        const int c0 = ((cc >> 2) << 3) + hh + (cc & 3), c1 = c0 + 1;  // this lane's half of the chunks
+        const float4 k0 = *reinterpret_cast<const float4*>(kb + jr * KR + 4 * c0);
+        const float4 k1 = *reinterpret_cast<const float4*>(kb + jr * KR + 4 * c1);
+#pragma unroll
+        for (int g = 0; g < DR_GMAX; ++g) {
+          if (g < G) {
+            const float4 qa = q4[g * CH + c0], qb = q4[g * CH + c1];
+            s0[g] = fmaf(qa.w, k0.w, fmaf(qa.z, k0.z, fmaf(qa.y, k0.y, fmaf(qa.x, k0.x, s0[g]))));
+            s1[g] = fmaf(qb.w, k1.w, fmaf(qb.z, k1.z, fmaf(qb.y, k1.y, fmaf(qb.x, k1.x, s1[g]))));
+          }
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < DR_GMAX; ++g) {
+        const float part = s0[g] + s1[g];
+        const float other = __shfl_xor_sync(0xffffffffu, part, 1);
+        s[g] = (lane & 1) ? other + part : part + other;
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < DR_GMAX; ++g) {
+      if (g >= G) break;
+      const float sc = jr < nv ? s[g] : -INFINITY;
+      const float mn = fmaxf(m[g], warp_max(sc));
+      const float corr = exp2f(m[g] - mn);
+      const float pz = jr < nv ? exp2f(sc - mn) : 0.f;
+      l[g] = fmaf(l[g], corr, lead ? pz : 0.f);
+#pragma unroll
+      for (int e = 0; e < E; ++e) o[g][e] *= corr;
+      m[g] = mn;
+      if (lead) pw[g * 16 + jr] = pz;
+    }
+    __syncwarp();
+    for (int j0 = 0; j0 < nv; j0 += 4) {
+      float4 pp[DR_GMAX];
+#pragma unroll
+      for (int g = 0; g < DR_GMAX; ++g)
+        if (g < G) pp[g] = *reinterpret_cast<const float4*>(pw + g * 16 + j0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (j0 + q < nv) {
+          float x[E];
+          const float* vr = vb + (j0 + q) * HD + lane * E;
+          if constexpr (E == 4) {
+            const float4 tt = *reinterpret_cast<const float4*>(vr);
+            x[0] = tt.x; x[1] = tt.y; x[2] = tt.z; x[3] = tt.w;
+          } else {
+            const float2 tt = *reinterpret_cast<const float2*>(vr);
+            x[0] = tt.x; x[1] = tt.y;
+          }
+#pragma unroll
+          for (int g = 0; g < DR_GMAX; ++g) {
+            if (g < G) {
+              const float pg = q == 0 ? pp[g].x : (q == 1 ? pp[g].y : (q == 2 ? pp[g].z : pp[g].w));
+#pragma unroll
+              for (int e = 0; e < E; ++e) o[g][e] = fmaf(pg, x[e], o[g][e]);
+            }
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) {
+      dr_arrive(&empty[sk]);
+      dr_arrive(&empty[sv]);
+    }
+    u += 2;
+  }
+#pragma unroll
+  for (int g = 0; g < DR_GMAX; ++g) l[g] = warp_sum(l[g]);
+
+  // merge the consumer warps: (m, l, o) per head, o staged in sX
+  float* sO = sX;  // [DR_CW][DR_GMAX][HD]
+  if (lane == 0) {
+#pragma unroll
+    for (int g = 0; g < DR_GMAX; ++g) {
+      sm_m[warp][g] = m[g];
+      sm_l[warp][g] = l[g];
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < DR_GMAX; ++g) {
+    if (g >= G) break;
+#pragma unroll
+    for (int e = 0; e < E; ++e) sO[(warp * DR_GMAX + g) * HD + lane * E + e] = o[g][e];
+  }
+  dr_csync();
+  const int WS = G * HD + ((2 * G + 3) & ~3);
+  constexpr int NT = DR_CW * 32;
+  float* mypart = P.apart + ((int64_t)kvh * ns + sp) * WS;
+  for (int i = threadIdx.x; i < G * HD; i += NT) {
+    const int g = i / HD, dd = i % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < DR_CW; ++w) M = fmaxf(M, sm_m[w][g]);
+    float Ls = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < DR_CW; ++w) {
+        if (sm_m[w][g] == -INFINITY) continue;
+        const float f = exp2f(sm_m[w][g] - M);
+        Ls = fmaf(sm_l[w][g], f, Ls);
+        O = fmaf(sO[(w * DR_GMAX + g) * HD + dd], f, O);
+      }
+    }
+    if (ns == 1) {
+      P.ao[(int64_t)(kvh * G + g) * HD + dd] = Ls > 0.f ? O / Ls : 0.f;
+    } else {
+      mypart[i] = O;
+      if (dd == 0) {
+        mypart[G * HD + g] = M;
+        mypart[G * HD + G + g] = Ls;
+      }
+    }
+  }
+  if (ns == 1) return;
+  dr_csync();
+  if (threadIdx.x == 0) {
+    int old;
+    asm volatile("fence.acq_rel.gpu;\n\tatom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                 : "=r"(old)
+                 : "l"(P.aticket + kvh)
+                 : "memory");
+    *s_last = old == ns - 1;
+  }
+  dr_csync();
+  if (!*s_last) return;
+
+  // last split CTA of this kv head: fold the splits in split order (runs of
+  // splits per thread, then the runs in order), write the heads' outputs
+  const float* base = P.apart + (int64_t)kvh * ns * WS;
+  const int nchunk = G * HD / 4;
+  const int nrun = max(1, min(ns, NT / nchunk));
+  float4* sred = reinterpret_cast<float4*>(sX + DR_CW * DR_GMAX * HD);
+  float2* sml = reinterpret_cast<float2*>(sred + nrun * nchunk);
+  for (int tt = threadIdx.x; tt < nrun * nchunk; tt += NT) {
+    const int i4 = tt % nchunk, run = tt / nchunk;
+    const int g = (4 * i4) / HD;
+    const int r0 = run * ns / nrun, r1 = (run + 1) * ns / nrun;
+    float M = -INFINITY, Ls = 0.f;
+    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = r0; s0 < r1; s0 += 8) {
+      float4 v[8];
+      float ms[8], ls[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const bool ok = s0 + q < r1;
+        const float* ps = base + (int64_t)(s0 + q) * WS;
+        v[q] = ok ? __ldcg(reinterpret_cast<const float4*>(ps) + i4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        ms[q] = ok ? __ldcg(ps + G * HD + g) : -INFINITY;
+        ls[q] = ok ? __ldcg(ps + G * HD + G + g) : 0.f;
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (ms[q] == -INFINITY) continue;
+        const float mn = fmaxf(M, ms[q]);
+        const float cf = exp2f(M - mn), f = exp2f(ms[q] - mn);
+        O.x = fmaf(v[q].x, f, O.x * cf);
+        O.y = fmaf(v[q].y, f, O.y * cf);
+        O.z = fmaf(v[q].z, f, O.z * cf);
+        O.w = fmaf(v[q].w, f, O.w * cf);
+        Ls = fmaf(ls[q], f, Ls * cf);
+        M = mn;
+      }
+    }
+    sred[run * nchunk + i4] = O;
+    sml[run * nchunk + i4] = make_float2(M, Ls);
+  }
+  dr_csync();
+  for (int i4 = threadIdx.x; i4 < nchunk; i4 += NT) {
+    float4 O = sred[i4];
+    float M = sml[i4].x, Ls = sml[i4].y;
+    for (int run = 1; run < nrun; ++run) {
+      const float2 ml = sml[run * nchunk + i4];
+      if (ml.x == -INFINITY) continue;
+      const float4 x = sred[run * nchunk + i4];
+      const float mn = fmaxf(M, ml.x);
+      const float cf = exp2f(M - mn), f = exp2f(ml.x - mn);
+      O.x = fmaf(x.x, f, O.x * cf);
+      O.y = fmaf(x.y, f, O.y * cf);
+      O.z = fmaf(x.z, f, O.z * cf);
+      O.w = fmaf(x.w, f, O.w * cf);
+      Ls = fmaf(ml.y, f, Ls * cf);
+      M = mn;
+    }
+    float* dst = P.ao + (int64_t)kvh * G * HD + 4 * i4;
+    dst[0] = Ls > 0.f ? O.x / Ls : 0.f;
+    dst[1] = Ls > 0.f ? O.y / Ls : 0.f;
+    dst[2] = Ls > 0.f ? O.z / Ls : 0.f;
+    dst[3] = Ls > 0.f ? O.w / Ls : 0.f;
+  }
+  if (threadIdx.x == 0) P.aticket[kvh] = 0;  // ready for the next layer
+}
+
+// ------------------------------------------------------------------ the step
+template <int HD>
+__global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t* xq = ring + DR_RING;
+  float4* fcol = reinterpret_cast<float4*>(xq + DR_XQ_BYTES);
+  float* sQ = reinterpret_cast<float*>(xq + DR_XQ_BYTES + DR_FCOL_BYTES);
+  float* sP = sQ + DR_GMAX * 128;
+  float* sKn = sP + DR_CW * DR_GMAX * 16;
+  float* sVn = sKn + 128;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sVn + 128);
+  uint64_t* empty = full + DR_SLOTS;
+  __shared__ float scr[DR_CW];
+  __shared__ float sm_m[DR_CW][DR_GMAX], sm_l[DR_CW][DR_GMAX];
+  __shared__ int s_last;
+  __shared__ unsigned long long s_key[DR_CW];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == DR_CW * 32) {
+    for (int s = 0; s < DR_SLOTS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (warp == DR_CW) {
+    dr_producer<HD>(P, ring, full, empty);
+    return;
+  }
+
+  // ---------------------------------------------------------------- consumers
+  const int G = gridDim.x, c = blockIdx.x;
+  int u = 0;
+  unsigned int target = 0;
+  const int nphase = 5 * P.L + 1;
+  for (int ph = 0; ph < nphase; ++ph) {
+    const int kind = dr_kind(P, ph), L = ph / 5;
+    if (ph > 0) {
+      target += (unsigned int)G;
+      dr_grid_wait(P, target);
+    }
+    if (kind == DP_ATTN) {
+      dr_attn<HD>(P, L, ring, full, empty, u, sQ, sP, sKn, sVn, reinterpret_cast<float*>(xq), sm_m, sm_l, &s_last);
+      dr_grid_arrive(P);
+      continue;
+    }
+    const DrG d = dr_gemv_desc(P, kind, L);
+    const DrLayer* ly = P.layers + (kind == DP_LM ? 0 : L);
+    float* hc = (L & 1) ? P.h1 : P.h0;  // this layer's residual
+    float* hp = (L & 1) ? P.h0 : P.h1;  // the previous layer's
+    switch (kind) {
+      case DP_QKV:
+        dr_stage(P, P.H, L == 0 ? DS_EMBED : DS_FOLD, hp, ly->in_norm, hc, xq, fcol, scr);
+        break;
+      case DP_O: dr_stage(P, P.qd, DS_F32, P.ao, nullptr, nullptr, xq, fcol, scr); break;
+      case DP_GU: dr_stage(P, P.H, DS_F32, hc, ly->post_norm, nullptr, xq, fcol, scr); break;
+      case DP_DOWN: dr_stage(P, P.F, DS_F32, P.act, nullptr, nullptr, xq, fcol, scr); break;
+      default: {
+        const int Lp = P.L - 1;
+        dr_stage(P, P.H, DS_FOLD, (Lp & 1) ? P.h1 : P.h0, P.final_norm, nullptr, xq, fcol, scr);
+      }
+    }
+    float* red = reinterpret_cast<float*>(xq + (((size_t)d.K * 3 + 15) & ~(size_t)15));
+    dr_gemv_run(P, d, ring, full, empty, xq, fcol, red, u, warp, lane);
+    dr_csync();
+
+    // epilogue over the CTA's tiles
+    const int n = d.s1 - d.s0;
+    const int t_lo = d.s0 / d.C;
+    const int ntile = n > 0 ? (d.s1 - 1) / d.C - t_lo + 1 : 0;
+    constexpr int NT = DR_CW * 32;
+    if (kind == DP_GU) {
+      for (int i = threadIdx.x; i < ntile * 8; i += NT) {
+        const int lt = i >> 3, r = i & 7;
+        const float gv = dr_tile_sum(d, red, lt, r), uv = dr_tile_sum(d, red, lt, r + 8);
+        P.act[(int64_t)(t_lo + lt) * 8 + r] = silu_mul(gv, uv);
+      }
+    } else if (kind == DP_LM) {
+      unsigned long long best = 0;
+      for (int i = threadIdx.x; i < ntile * 16; i += NT) {
+        const int lt = i >> 4, r = i & 15;
+        const int row = (t_lo + lt) * 16 + r;
+        const float v = dr_tile_sum(d, red, lt, r);
+        P.logits[row] = v;
+        const unsigned long long k = dr_key(v, row);
+        best = k > best ? k : best;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long ok = __shfl_xor_sync(0xffffffffu, best, o);
+        best = ok > best ? ok : best;
+      }
+      if (lane == 0) s_key[warp] = best;
+      dr_csync();
+      if (threadIdx.x == 0) {
+        unsigned long long b = 0;
+        for (int w = 0; w < DR_CW; ++w) b = s_key[w] > b ? s_key[w] : b;
+        if (b) atomicMax(P.amax, b);
+        int old;
+        asm volatile("fence.acq_rel.gpu;\n\tatom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                     : "=r"(old)
+                     : "l"(P.lm_ticket)
+                     : "memory");
+        if (old == G - 1) {  // every CTA's maximum is in: the step's token
+          const unsigned long long k = atomicAdd(P.amax, 0ull);
+          const int32_t tok = (int32_t)(~(uint32_t)(k & 0xFFFFFFFFull));
+          P.argmax[0] = tok;
+          if (P.gen) {
+            const int step = *P.ctr;
+            P.ids[0] = tok;
+            P.pos[0] += 1;
+            if (step < P.hist_cap) P.hist[step] = tok;
+            *P.ctr = step + 1;
+          }
+          *P.amax = 0ull;
+          *P.lm_ticket = 0;
+        }
+      }
+      continue;  // the last phase: no arrival
+    } else {
+      for (int i = threadIdx.x; i < ntile * 16; i += NT) {
+        const int lt = i >> 4, r = i & 15;
+        const int tile = t_lo + lt, row = tile * 16 + r;
+        const float v = dr_tile_sum(d, red, lt, r);
+        if (kind == DP_QKV) {
+          P.qkv[row] = v;
+        } else if (kind == DP_O) {
+          hc[row] = __ldcg(hc + row) + v;
+        } else {  // DP_DOWN: this CTA's partial of the tile into its slot
+          const long long S = (long long)d.T * d.C;
+          const int slot = c - dr_cta_of((long long)tile * d.C, S);
+          P.pres[(int64_t)slot * P.H + row] = v;
+        }
+      }
+    }
+    dr_grid_arrive(P);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+size_t dr_apart_floats(int nkv, int nsplit, int hd) {
+  return (size_t)nkv * nsplit * (DR_GMAX * hd + 2 * DR_GMAX + 4);
+}
+
+int dr_nsplit(int G, int nkv) { return std::max(1, std::min(DR_MAXSPLIT, G / std::max(1, nkv))); }
+
+bool dr_supported(int H, int nh, int nkv, int hd, int F, int V, int page, const char** why) {
+  auto no = [&](const char* w) {
+    if (why) *why = w;
+    return false;
+  };
+  if (hd != 64 && hd != 128) return no("head_dim must be 64 or 128");
+  if (nkv < 1 || nh % nkv != 0 || nh / nkv > DR_GMAX) return no("more than 4 q heads per kv head");
+  const int qd = nh * hd, nqkv = qd + 2 * nkv * hd;
+  if (H % DR_CK || qd % DR_CK || F % DR_CK) return no("hidden, q width and FFN width must be multiples of 512");
+  if (nqkv % 16 || H % 16 || V % 16) return no("output widths must be multiples of 16");
+  if (std::max({H, qd, F}) > 16384 || H > 8192) return no("inputs too wide for the staging");
+  if (page % 16) return no("KV page must be a multiple of 16 positions");
+  const int G = num_sms();
+  if (nkv > G) return no("more kv heads than SMs");
+  // digits + per-warp tile sums fit the staging area in every phase
+  auto fits = [&](int K, int T, bool split) {
+    const int C = K / DR_CK;
+    const int tiles = split ? ((int)((long long)T * C / G) + C - 1) / C + 2 : (T + G - 1) / G + 1;
+    return (size_t)K * 3 + 16 + (size_t)tiles * DR_CW * 16 * 4 <= (size_t)DR_XQ_BYTES;
+  };
+  if (!fits(H, nqkv / 16, false) || !fits(qd, H / 16, false) || !fits(H, F / 8, false) || !fits(F, H / 16, true) ||
+      !fits(H, V / 16, false))
+    return no("staging area too small");
+  // the down projection is split evenly over min(G, S) CTAs: a tile of C
+  // stages meets at most ceil((C - 1) / per) + 1 <= DR_NS of them
+  {
+    const int C = F / DR_CK;
+    const long long S = (long long)(H / 16) * C;
+    const long long per = S / std::min((long long)G, S);
+    if ((C - 2 + per) / per + 1 > DR_NS) return no("down tiles would span too many CTAs");
+  }
+  return true;
+}
+
+template <int HD>
+static int dr_attr() {
+  Q8_CUDA(cudaFuncSetAttribute(k_decode_ring<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, DR_SMEM));
+  return Q8_OK;
+}
+
+int dr_prepare(int hd, int* grid) {
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  int dev = 0, coop = 0, per_sm = 0;
+  Q8_CUDA(cudaGetDevice(&dev));
+  Q8_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
+  if (hd == 128) {
+    Q8_TRY(dr_attr<128>());
+    Q8_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_ring<128>, DR_THREADS, DR_SMEM));
+  } else {
+    Q8_TRY(dr_attr<64>());
+    Q8_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_ring<64>, DR_THREADS, DR_SMEM));
+  }
+  *grid = (coop && per_sm >= 1) ? num_sms() : 0;
+  return Q8_OK;
+}
+
+int dr_launch(const DrParams& p, int grid, cudaStream_t st) {
+  Q8_CHECK_ARG(grid > 0, "decode ring: not prepared");
+  Q8_CUDA(cudaMemsetAsync(p.bar, 0, sizeof(unsigned int), st));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(DR_THREADS);
+  cfg.dynamicSmemBytes = DR_SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = p.hd == 128 ? cudaLaunchKernelEx(&cfg, k_decode_ring<128>, p)
+                              : cudaLaunchKernelEx(&cfg, k_decode_ring<64>, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("launch k_decode_ring: %s", cudaGetErrorString(e));
+    return Q8_ERR_CUDA;
+  }
+  return Q8_OK;
+}
+
+}  // namespace q8

@@ -1,0 +1,78 @@
+// Parameters of the weight-ring decode step (q8_decode_ring.cu) shared with
+// the model runtime that fills them.
+#pragma once
+#include "q8_common.cuh"
+
+namespace q8 {
+
+constexpr int DR_CW = 8;                         // consumer warps
+constexpr int DR_THREADS = (DR_CW + 1) * 32;     // + one producer warp
+constexpr int DR_SLOTS = 2 * DR_CW;              // ring slots, two per consumer warp
+constexpr int DR_CK = 512;                       // code bytes of one row in a GEMV stage
+constexpr int DR_RS = DR_CK + 16;                // padded row stride in shared memory
+constexpr int DR_SLOT_BYTES = 16 * DR_RS + 16 * 16;  // 16 code rows + their 16 x 8 group scales
+constexpr int DR_XQ_BYTES = 48 * 1024;           // activation digits + per-warp tile sums
+constexpr int DR_NS = 4;                         // partial slots of a down tile shared by CTAs
+constexpr int DR_GMAX = 4;                       // q heads per kv head
+constexpr int DR_MAXSPLIT = 128;                 // attention context splits per kv head
+
+struct DrLayer {
+  const uint8_t* qkv;  // packed [nq*hd + 2*nkv*hd rows][H]
+  const uint8_t* o;    // [H rows][nq*hd]
+  const uint8_t* gu;   // [2F rows][H]: F gate rows then F up rows
+  const uint8_t* down; // [H rows][F]
+  const uint16_t* in_norm;
+  const uint16_t* post_norm;
+  const uint16_t* q_norm;  // Qwen3 QK-norm (null otherwise)
+  const uint16_t* k_norm;
+  float* kp;           // this layer's paged K / V pools [pages][nkv][page][hd]
+  float* vp;
+};
+
+struct DrParams {
+  int H, nh, nkv, hd, qd, nqkv, F, V, L;
+  float eps;
+  const DrLayer* layers;       // device array [L]
+  const uint8_t* embed;        // packed [vocab][H]
+  const uint8_t* lm_head;      // packed [V][H]
+  const uint16_t* final_norm;
+  int32_t* ids;                // [1] token of the step (the generate epilogue writes the next one)
+  int32_t* pos;                // [1] its position
+  const int32_t* seq;          // [1] its KV sequence slot
+  const float* inv_freq;       // [hd/2]
+  int page;
+  const int32_t* bt;           // block table [max_seqs][max_pages]
+  int max_pages;
+  // work buffers, written inside the launch and read by other CTAs with
+  // L2-coherent loads
+  float* h0;                   // residual of even layers [H]
+  float* h1;                   // residual of odd layers [H]
+  float* pres;                 // down-projection partial slots [DR_NS][H]
+  float* qkv;                  // [nqkv]
+  float* ao;                   // attention output [qd]
+  float* act;                  // SwiGLU output [F]
+  float* logits;               // [V]
+  float* apart;                // attention split partials [nkv][nsplit][GMAX*hd + 2*GMAX]
+  int* aticket;                // [nkv], zero at rest
+  int nsplit;
+  unsigned long long* amax;    // packed (ordered value, ~index) of the step's argmax, zero at rest
+  int* lm_ticket;              // zero at rest
+  int32_t* argmax;             // [1]
+  int gen;                     // generate epilogue: ids = argmax, pos += 1, hist[ctr] = argmax, ctr += 1
+  int32_t* hist;
+  int32_t* ctr;
+  int hist_cap;
+  unsigned int* bar;           // grid barrier arrivals (zeroed before each launch)
+  int* status;                 // device status word (zero at rest)
+};
+
+// Host side (q8_decode_ring.cu).
+// Whether the ring step supports these model dimensions on this device
+// (one sequence, one GPU); *why gets the reason when it does not.
+bool dr_supported(int H, int nh, int nkv, int hd, int F, int V, int page, const char** why);
+int dr_prepare(int hd, int* grid);  // kernel attributes, residency check; grid = CTAs (one per SM)
+size_t dr_apart_floats(int nkv, int nsplit, int hd);
+int dr_nsplit(int G, int nkv);
+int dr_launch(const DrParams& p, int grid, cudaStream_t st);
+
+}  // namespace q8

@@ -9,7 +9,7 @@
 //   Acts bump arena            src/llama_common.mojo:578-606
 //   SafeTensors                src/safetensors.mojo:17-96
 #include "q8_allreduce.h"
-#include "q8_decode_mk.h"
+#include "q8_decode_ring.h"
 #include "q8_kernels.h"
 #include "safetensors.h"
 
@@ -207,23 +207,15 @@ struct q8_ctx {
   size_t part_floats = 0;
   __half *xs_in = nullptr, *xs_ao = nullptr, *xs_act = nullptr;
   bool tc = false;  // tensor-core GEMM for prefill batches (every K a multiple of 512)
-  // persistent decode step (one GPU, <= MK_BMAX tokens)
-  bool mk = false;
-  int mk_vec = 16, mk_G = 0;
-  MkLayer* mk_layers = nullptr;
-  float *mk_hB = nullptr, *mk_pqkv = nullptr, *mk_pres = nullptr, *mk_ao = nullptr, *mk_act = nullptr;
-  float* mk_apart = nullptr;
-  int mk_bmax = 0;  // step batch limit of the persistent step
-  unsigned long long* mk_key = nullptr;
-  int* mk_ticket = nullptr;
-  unsigned int* mk_bar = nullptr;
-  int* mk_status = nullptr;
-  int* mk_status_pin = nullptr;
-  double mk_wbytes = 0;  // weight bytes one step streams
-  unsigned long long* mk_ts = nullptr;  // phase trace of the last profiled step
-  unsigned long long* mk_ts2 = nullptr;
-  bool mk_traced = false;
-  double mk_kv_bytes = 0;
+  // weight-ring decode step (one GPU, one sequence): q8_decode_ring.cu
+  bool dr = false;
+  int dr_grid = 0, dr_nsplit = 1;
+  DrLayer* dr_layers = nullptr;
+  float *dr_h1 = nullptr, *dr_pres = nullptr, *dr_apart = nullptr;
+  int *dr_aticket = nullptr, *dr_lm_ticket = nullptr, *dr_status = nullptr, *dr_status_pin = nullptr;
+  unsigned long long* dr_amax = nullptr;
+  unsigned int* dr_bar = nullptr;
+  double dr_wbytes = 0;  // weight bytes one step streams
   float *xn32 = nullptr, *ao32 = nullptr, *act32 = nullptr;  // f32 copies of the GEMV inputs
   float *am_val = nullptr, *am_gval = nullptr, *lg_gather = nullptr;
   int32_t *am_idx = nullptr, *am_gidx = nullptr;
@@ -299,6 +291,29 @@ static int allreduce(q8_ctx* c, float* buf, size_t n) {
 // batch is too large for it, so the caller keeps NCCL + the RMSNorm kernel.
 static bool p2p_fits(q8_ctx* c, int T) { return c->ar.ok && (int64_t)T * c->H <= c->ar.slot; }
 
+// Whether a step of T tokens runs as one weight-ring launch (one decode
+// token, greedy, the whole vocabulary on this GPU).
+static bool ring_ok(q8_ctx* c, int T, bool blocks, int lrow0, int lrows) {
+  return c->dr && T == 1 && !blocks && lrow0 == 0 && lrows == 1 && !(c->samp_temp > 0.f);
+}
+
+// One weight-ring decode step for the token in ids_d / pos_d / seq_d; with
+// gen, the launch also feeds its argmax back (k_step_end's work).
+static int ring_step(q8_ctx* c, bool gen) {
+  DrParams p{};
+  p.H = c->H; p.nh = c->nh; p.nkv = c->nkv; p.hd = c->hd; p.qd = c->qd; p.nqkv = c->qd + 2 * c->kvd;
+  p.F = c->F; p.V = c->V; p.L = c->cfg.layers; p.eps = c->cfg.eps;
+  p.layers = c->dr_layers; p.embed = c->embed; p.lm_head = c->lm_head; p.final_norm = c->final_norm;
+  p.ids = c->ids_d; p.pos = c->pos_d; p.seq = c->seq_d; p.inv_freq = c->inv_freq_d;
+  p.page = c->page; p.bt = c->bt_d; p.max_pages = c->max_pages;
+  p.h0 = c->h; p.h1 = c->dr_h1; p.pres = c->dr_pres; p.qkv = c->qkv; p.ao = c->ao32; p.act = c->act32;
+  p.logits = c->logits; p.apart = c->dr_apart; p.aticket = c->dr_aticket; p.nsplit = c->dr_nsplit;
+  p.amax = c->dr_amax; p.lm_ticket = c->dr_lm_ticket; p.argmax = c->argmax_d;
+  p.gen = gen ? 1 : 0; p.hist = c->hist_d; p.ctr = c->ctr_d; p.hist_cap = c->hist_cap;
+  p.bar = c->dr_bar; p.status = c->dr_status;
+  return dr_launch(p, c->dr_grid, c->st);
+}
+
 // Runs T tokens whose ids/pos/seq (and query blocks, when qb_tok0 != null) are
 // already in the device buffers.  Produces logits + argmax for token rows
 // [lrow0, lrow0 + lrows).  kv_ctx_hint bounds the context for split sizing.
@@ -308,27 +323,8 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
   const int nqkv = c->qd + 2 * c->kvd;
   cudaStream_t st = c->st;
   const bool tp = c->tp_size > 1;
-  if (c->mk && !blocks && T <= c->mk_bmax && lrow0 == 0 && lrows == T && !(c->samp_temp > 0.f)) {
-    MkParams p{};
-    p.B = T; p.H = H; p.nh = c->nh; p.nkv = c->nkv; p.hd = c->hd; p.qd = c->qd; p.nqkv = nqkv; p.F = c->F;
-    p.V = c->V; p.L = c->cfg.layers; p.eps = c->cfg.eps;
-    p.layers = c->mk_layers; p.embed = c->embed; p.lm_head = c->lm_head; p.final_norm = c->final_norm;
-    p.ids = c->ids_d; p.pos = c->pos_d; p.seq = c->seq_d; p.inv_freq = c->inv_freq_d;
-    p.page = c->page; p.bt = c->bt_d; p.max_pages = c->max_pages;
-    p.hA = c->h; p.hB = c->mk_hB; p.pqkv = c->mk_pqkv; p.pres = c->mk_pres; p.ao = c->mk_ao; p.act = c->mk_act;
-    p.logits = c->logits; p.amax_key = c->mk_key; p.argmax = c->argmax_d;
-    p.apart = c->mk_apart; p.ticket = c->mk_ticket;
-    p.nsplit = std::max(1, std::min(MK_MAXSPLIT, c->mk_G / (T * c->nkv)));
-    p.bar = c->mk_bar; p.status = c->mk_status;
-    {
-      const char* e = getenv("Q8_MK_PF");  // L2 prefetch budget per CTA per phase (KB)
-      p.pf_bytes = (e ? atoi(e) : 256) * 1024;
-    }
-    p.ts = c->profiling ? c->mk_ts : nullptr;
-    p.ts2 = c->profiling ? c->mk_ts2 : nullptr;
-    c->mk_traced = c->profiling;
-    c->mk_kv_bytes = kv_bytes_hint;
-    PROF(c, "decode_step", c->mk_wbytes + kv_bytes_hint, mk_launch(p, c->mk_vec, c->mk_G, st));
+  if (ring_ok(c, T, blocks, lrow0, lrows)) {
+    PROF(c, "decode_step", c->dr_wbytes + kv_bytes_hint, ring_step(c, false));
     return Q8_OK;
   }
   PROF(c, "embed", (double)T * (q8_row_bytes(H) + H * 4.0),
@@ -523,17 +519,18 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
   return Q8_OK;
 }
 
-// The persistent decode step's status word: queued copy to pinned memory
+// Device status words (bounded waits of the ring step, the tensor-core GEMM,
+// the decode attention and the P2P exchange): queued copies to pinned memory
 // with the call's other results, checked after the call's synchronize.
-static int mk_status_copy(q8_ctx* c) {
+static int status_copy(q8_ctx* c) {
   for (int i = 0; i < 2; ++i)
     Q8_CUDA(cudaMemcpyAsync(c->dev_err_pin + i, c->dev_err[i], 4, cudaMemcpyDeviceToHost, c->st));
-  if (c->mk) Q8_CUDA(cudaMemcpyAsync(c->mk_status_pin, c->mk_status, 4, cudaMemcpyDeviceToHost, c->st));
+  if (c->dr) Q8_CUDA(cudaMemcpyAsync(c->dr_status_pin, c->dr_status, 4, cudaMemcpyDeviceToHost, c->st));
   if (c->ar.ok) Q8_CUDA(cudaMemcpyAsync(c->ar_status_pin, c->ar.status, 4, cudaMemcpyDeviceToHost, c->st));
   return Q8_OK;
 }
 
-static int mk_status_check(q8_ctx* c) {
+static int status_check(q8_ctx* c) {
   if (c->dev_err_pin[0] != 0 || c->dev_err_pin[1] != 0) {
     // a bounded wait gave up: the call's results are not trusted.  Clear the
     // words so that later waits in those kernels run to their full bound.
@@ -553,14 +550,16 @@ static int mk_status_check(q8_ctx* c) {
     set_error("tensor-parallel allreduce: a peer flag wait timed out (device status %d)", v);
     return Q8_ERR_COMM;
   }
-  if (!c->mk || *c->mk_status_pin == 0) return Q8_OK;
-  const int v = *c->mk_status_pin;
-  *c->mk_status_pin = 0;
-  // the grid drained early: clear the status word and the split tickets
-  Q8_CUDA(cudaMemsetAsync(c->mk_status, 0, 4, c->st));
-  Q8_CUDA(cudaMemsetAsync(c->mk_ticket, 0, (size_t)MK_BMAX * c->nkv * 4, c->st));
+  if (!c->dr || *c->dr_status_pin == 0) return Q8_OK;
+  const int v = *c->dr_status_pin;
+  *c->dr_status_pin = 0;
+  // the grid drained early: clear the status word and the step's tickets
+  Q8_CUDA(cudaMemsetAsync(c->dr_status, 0, 4, c->st));
+  Q8_CUDA(cudaMemsetAsync(c->dr_aticket, 0, (size_t)c->nkv * 4, c->st));
+  Q8_CUDA(cudaMemsetAsync(c->dr_lm_ticket, 0, 4, c->st));
+  Q8_CUDA(cudaMemsetAsync(c->dr_amax, 0, 8, c->st));
   Q8_CUDA(cudaStreamSynchronize(c->st));
-  set_error("decode step: a grid barrier wait timed out (device status %d)", v);
+  set_error("decode step: a bounded device wait timed out (device status %d)", v);
   return Q8_ERR_TIMEOUT;
 }
 
@@ -680,14 +679,14 @@ static int destroy_impl(q8_ctx* c) {
   void* ptrs[] = {c->warena, c->kpool, c->vpool, c->bt_d, c->inv_freq_d, c->ids_d, c->pos_d, c->seq_d,
                   c->qb_tok0_d, c->qb_len_d, c->argmax_d, c->hist_d, c->ctr_d, c->ticket_d, c->h, c->qkv, c->ypart,
                   c->logits, c->part, c->xs_in, c->xs_ao, c->xs_act, c->xn32, c->ao32, c->act32, c->am_val, c->am_gval, c->lg_gather,
-                  c->am_idx, c->am_gidx, c->mk_hB, c->mk_pqkv, c->mk_pres, c->mk_ao, c->mk_act,
-                  c->mk_apart, c->mk_key, c->mk_ticket, c->mk_bar, c->mk_status, c->mk_layers, c->mk_ts, c->mk_ts2,
+                  c->am_idx, c->am_gidx, c->dr_layers, c->dr_h1, c->dr_pres, c->dr_apart, c->dr_aticket,
+                  c->dr_lm_ticket, c->dr_status, c->dr_amax, c->dr_bar,
                   c->samp_ws, c->samp_u, c->samp_logits};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   if (c->pin) cudaFreeHost(c->pin);
   if (c->dev_err_pin) cudaFreeHost(c->dev_err_pin);
-  if (c->mk_status_pin) cudaFreeHost(c->mk_status_pin);
+  if (c->dr_status_pin) cudaFreeHost(c->dr_status_pin);
   if (c->st) cudaStreamDestroy(c->st);
   delete c;
   return Q8_OK;
@@ -911,60 +910,46 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
   if ((s = gemv_d_prepare(std::max({ceil_div(c->qd + 2 * c->kvd, 16), ceil_div(H, 16), ceil_div(c->F, 8),
                                     ceil_div(c->V_loc, 16)})))) return bail(s);
 
-  // ---- persistent decode step (opt-in, Q8_MK=1): one GPU, hd 64/128,
-  // <= MK_GMAX q heads per kv head, every K a multiple of 256
+  // ---- weight-ring decode step for one-sequence greedy decode on one GPU
+  // (default; Q8_RING=0 keeps those steps on the per-operation kernels)
   {
-    const char* e = getenv("Q8_MK");
-    const int nqkv = c->qd + 2 * c->kvd;
-    const bool shape_ok = tp_size == 1 && (c->hd == 64 || c->hd == 128) && c->nh % c->nkv == 0 &&
-                          c->nh / c->nkv <= MK_GMAX && H % 256 == 0 && c->qd % 256 == 0 && c->F % 256 == 0 &&
-                          (size_t)MK_BMAX * std::max(H, c->qd) * 4 <= (size_t)MK_XS_BYTES;
-    if (e && e[0] == '1' && shape_ok) {
-      c->mk_vec = (H % 512 == 0 && c->qd % 512 == 0 && c->F % 512 == 0) ? 16 : 8;
-      c->mk_G = num_sms();
-      bool ok = false;
-      if ((s = mk_check_residency(c->hd, c->mk_vec, c->mk_G, &ok))) return bail(s);
-      const int sl_qkv = mk_slots(H, nqkv, false, false, c->mk_G);
-      const int sl_res = std::max(mk_slots(c->qd, H, false, false, c->mk_G), mk_slots(c->F, H, false, false, c->mk_G));
-      // unit arithmetic runs in 32 bits: U * G < 2^31 for every phase
-      const double umax = std::max({(double)ceil_div(nqkv, 16) * (H / 64), (double)ceil_div(H, 16) * (c->qd / 64),
-                                    (double)ceil_div(c->F, 8) * (H / 64), (double)ceil_div(H, 16) * (c->F / 64),
-                                    (double)ceil_div(c->V, 16) * (H / 64)});
-      c->mk_bmax = mk_max_batch(H, c->qd, c->F);
-      if (ok && c->mk_bmax >= 1 && sl_qkv <= 16 && sl_res <= 16 && umax * c->mk_G < 2147483648.0) {
-        const size_t apart = (size_t)(c->mk_G + MK_BMAX * c->nkv) * (MK_GMAX * c->hd + 2 * MK_GMAX);
-        if ((s = dmalloc((void**)&c->mk_hB, (size_t)MK_BMAX * H * 4))) return bail(s);
-        if ((s = dmalloc((void**)&c->mk_pqkv, (size_t)sl_qkv * MK_BMAX * nqkv * 4))) return bail(s);
-        if ((s = dmalloc((void**)&c->mk_pres, (size_t)sl_res * MK_BMAX * H * 4))) return bail(s);
-        if ((s = dmalloc((void**)&c->mk_ao, (size_t)MK_BMAX * c->qd * 4))) return bail(s);
-        if ((s = dmalloc((void**)&c->mk_act, (size_t)MK_BMAX * c->F * 4))) return bail(s);
-        if ((s = dmalloc((void**)&c->mk_apart, apart * 4))) return bail(s);
-        if ((s = dmalloc((void**)&c->mk_key, MK_BMAX * 8))) return bail(s);
-        if ((s = dmalloc((void**)&c->mk_ticket, (size_t)MK_BMAX * c->nkv * 4))) return bail(s);
-        if ((s = dmalloc((void**)&c->mk_bar, 4))) return bail(s);
-        if ((s = dmalloc((void**)&c->mk_status, 4))) return bail(s);
-        if ((s = dmalloc((void**)&c->mk_layers, sizeof(MkLayer) * C.layers))) return bail(s);
-        if ((s = dmalloc((void**)&c->mk_ts, sizeof(unsigned long long) * (5 * C.layers + 4)))) return bail(s);
-        if ((s = dmalloc((void**)&c->mk_ts2, sizeof(unsigned long long) * 4 * (5 * C.layers + 4)))) return bail(s);
-        if (cudaMemset(c->mk_ticket, 0, (size_t)MK_BMAX * c->nkv * 4) != cudaSuccess ||
-            cudaMemset(c->mk_status, 0, 4) != cudaSuccess)
-          return bail((set_error("decode step state clear failed"), Q8_ERR_CUDA));
-        if (cudaMallocHost((void**)&c->mk_status_pin, 4) != cudaSuccess)
-          return bail((set_error("cudaMallocHost failed"), Q8_ERR_OOM));
-        *c->mk_status_pin = 0;
-        std::vector<MkLayer> ml(C.layers);
-        for (int L = 0; L < C.layers; ++L) {
-          const LayerW& w = c->layers[L];
-          ml[L] = MkLayer{w.qkv, w.o, w.gu, w.down, w.in_norm, w.post_norm, w.q_norm, w.k_norm,
-                          c->kpool + (size_t)L * c->layer_kv, c->vpool + (size_t)L * c->layer_kv};
-        }
-        if (cudaMemcpy(c->mk_layers, ml.data(), sizeof(MkLayer) * C.layers, cudaMemcpyHostToDevice) != cudaSuccess)
-          return bail((set_error("decode step layer table upload failed"), Q8_ERR_CUDA));
-        c->mk_wbytes = (double)C.layers * ((double)nqkv * q8_row_bytes(H) + (double)H * q8_row_bytes(c->qd) +
-                                           2.0 * c->F * q8_row_bytes(H) + (double)H * q8_row_bytes(c->F)) +
-                       (double)c->V * q8_row_bytes(H);
-        c->mk = true;
+    const char* e = getenv("Q8_RING");
+    const char* why = nullptr;
+    if (!(e && e[0] == '0') && tp_size == 1 &&
+        dr_supported(H, c->nh, c->nkv, c->hd, c->F, c->V, c->page, &why)) {
+      if ((s = dr_prepare(c->hd, &c->dr_grid))) return bail(s);
+    }
+    if (c->dr_grid > 0) {
+      const int nqkv = c->qd + 2 * c->kvd;
+      c->dr_nsplit = dr_nsplit(c->dr_grid, c->nkv);
+      if ((s = dmalloc((void**)&c->dr_h1, (size_t)H * 4))) return bail(s);
+      if ((s = dmalloc((void**)&c->dr_pres, (size_t)DR_NS * H * 4))) return bail(s);
+      if ((s = dmalloc((void**)&c->dr_apart, dr_apart_floats(c->nkv, c->dr_nsplit, c->hd) * 4))) return bail(s);
+      if ((s = dmalloc((void**)&c->dr_aticket, (size_t)c->nkv * 4))) return bail(s);
+      if ((s = dmalloc((void**)&c->dr_lm_ticket, 4))) return bail(s);
+      if ((s = dmalloc((void**)&c->dr_status, 4))) return bail(s);
+      if ((s = dmalloc((void**)&c->dr_amax, 8))) return bail(s);
+      if ((s = dmalloc((void**)&c->dr_bar, 4))) return bail(s);
+      if ((s = dmalloc((void**)&c->dr_layers, sizeof(DrLayer) * C.layers))) return bail(s);
+      if (cudaMemset(c->dr_aticket, 0, (size_t)c->nkv * 4) != cudaSuccess ||
+          cudaMemset(c->dr_lm_ticket, 0, 4) != cudaSuccess || cudaMemset(c->dr_status, 0, 4) != cudaSuccess ||
+          cudaMemset(c->dr_amax, 0, 8) != cudaSuccess)
+        return bail((set_error("decode step state clear failed"), Q8_ERR_CUDA));
+      if (cudaMallocHost((void**)&c->dr_status_pin, 4) != cudaSuccess)
+        return bail((set_error("cudaMallocHost failed"), Q8_ERR_OOM));
+      *c->dr_status_pin = 0;
+      std::vector<DrLayer> dl(C.layers);
+      for (int L = 0; L < C.layers; ++L) {
+        const LayerW& w = c->layers[L];
+        dl[L] = DrLayer{w.qkv, w.o, w.gu, w.down, w.in_norm, w.post_norm, w.q_norm, w.k_norm,
+                        c->kpool + (size_t)L * c->layer_kv, c->vpool + (size_t)L * c->layer_kv};
       }
+      if (cudaMemcpy(c->dr_layers, dl.data(), sizeof(DrLayer) * C.layers, cudaMemcpyHostToDevice) != cudaSuccess)
+        return bail((set_error("decode step layer table upload failed"), Q8_ERR_CUDA));
+      c->dr_wbytes = (double)C.layers * ((double)nqkv * q8_row_bytes(H) + (double)H * q8_row_bytes(c->qd) +
+                                         2.0 * c->F * q8_row_bytes(H) + (double)H * q8_row_bytes(c->F)) +
+                     (double)c->V * q8_row_bytes(H);
+      c->dr = true;
     }
   }
 
@@ -1278,7 +1263,6 @@ static int forward_impl(q8_ctx* c, const int32_t* ids, int s, int seq, float* lo
     }
   c->prof.clear();
   c->ev_used = 0;
-  c->mk_traced = false;
   int done = 0;
   while (done < s) {
     const int T = std::min(s - done, c->max_tokens);
@@ -1318,9 +1302,9 @@ static int forward_impl(q8_ctx* c, const int32_t* ids, int s, int seq, float* lo
   }
   if (logits) Q8_TRY(gather_logits(c, 1, logits));
   if (argmax) Q8_CUDA(cudaMemcpyAsync(argmax, c->argmax_d, 4, cudaMemcpyDeviceToHost, c->st));
-  Q8_TRY(mk_status_copy(c));
+  Q8_TRY(status_copy(c));
   Q8_CUDA(cudaStreamSynchronize(c->st));
-  Q8_TRY(mk_status_check(c));
+  Q8_TRY(status_check(c));
   return Q8_OK;
 }
 
@@ -1351,7 +1335,6 @@ static int forward_hidden_impl(q8_ctx* c, const int32_t* ids, int s, int seq, in
   c->cfg.layers = layer + 1;  // run layers [0, layer]
   c->prof.clear();
   c->ev_used = 0;
-  c->mk_traced = false;
   int items = nqb * c->nkv;
   int nsplit = std::max(1, std::min(ceil_div(2 * num_sms(), items), ceil_div(pos0 + T, 128)));
   nsplit = std::max(1, std::min(nsplit, 1024 / std::max(1, items)));
@@ -1362,9 +1345,9 @@ static int forward_hidden_impl(q8_ctx* c, const int32_t* ids, int s, int seq, in
     Q8_TRY(rmsnorm_launch(c->h, c->ypart, c->final_norm, T, c->H, c->cfg.eps, nullptr, nullptr, nullptr, c->st));
   }
   Q8_CUDA(cudaMemcpyAsync(out, c->h, (size_t)T * c->H * 4, cudaMemcpyDeviceToHost, c->st));
-  Q8_TRY(mk_status_copy(c));
+  Q8_TRY(status_copy(c));
   Q8_CUDA(cudaStreamSynchronize(c->st));
-  Q8_TRY(mk_status_check(c));
+  Q8_TRY(status_check(c));
   return Q8_OK;
 }
 
@@ -1374,6 +1357,10 @@ int q8_forward_hidden(q8_ctx* ctx, const int32_t* ids, int s, int seq, int layer
 
 // Records the decode step for B sequences (one token each) on the stream.
 static int decode_body(q8_ctx* c, int B, bool gen_epilogue, double kvb) {
+  if (ring_ok(c, B, false, 0, B)) {  // one launch, argmax fed back inside it
+    PROF(c, "decode_step", c->dr_wbytes + kvb, ring_step(c, gen_epilogue));
+    return Q8_OK;
+  }
   Q8_TRY(run_tokens(c, B, false, B, 1, decode_nsplit(c, B), 0, B, kvb));
   if (gen_epilogue) {
     k_step_end<<<1, std::max(32, ((B + 31) / 32) * 32), 0, c->st>>>(c->argmax_d, c->ids_d, c->pos_d, c->hist_d,
@@ -1450,7 +1437,6 @@ static int decode_impl(q8_ctx* c, const int32_t* ids, const int32_t* seqs, int B
   Q8_TRY(stage_decode(c, ids, seqs, B, lens));
   c->prof.clear();
   c->ev_used = 0;
-  c->mk_traced = false;
   if (c->profiling) {
     Q8_TRY(decode_body(c, B, false, kv_read_bytes(c, lens)));
   } else {
@@ -1460,9 +1446,9 @@ static int decode_impl(q8_ctx* c, const int32_t* ids, const int32_t* seqs, int B
   }
   if (logits) Q8_TRY(gather_logits(c, B, logits));
   if (argmax) Q8_CUDA(cudaMemcpyAsync(argmax, c->argmax_d, (size_t)B * 4, cudaMemcpyDeviceToHost, c->st));
-  Q8_TRY(mk_status_copy(c));
+  Q8_TRY(status_copy(c));
   Q8_CUDA(cudaStreamSynchronize(c->st));
-  Q8_TRY(mk_status_check(c));
+  Q8_TRY(status_check(c));
   for (int b = 0; b < B; ++b) c->n_cached[seqs[b]] += 1;
   return Q8_OK;
 }
@@ -1492,9 +1478,9 @@ static int generate_impl(q8_ctx* c, const int32_t* first, const int32_t* seqs, i
   Q8_TRY(get_graph(c, B, true, &ge));
   for (int i = 0; i < steps; ++i) Q8_CUDA(cudaGraphLaunch(ge, c->st));
   if (out) Q8_CUDA(cudaMemcpyAsync(out, c->hist_d, (size_t)steps * B * 4, cudaMemcpyDeviceToHost, c->st));
-  Q8_TRY(mk_status_copy(c));
+  Q8_TRY(status_copy(c));
   Q8_CUDA(cudaStreamSynchronize(c->st));
-  Q8_TRY(mk_status_check(c));
+  Q8_TRY(status_check(c));
   for (int b = 0; b < B; ++b) c->n_cached[seqs[b]] += steps;
   return Q8_OK;
 }
@@ -1591,59 +1577,6 @@ int q8_profile(const q8_ctx* ctx, int cap, const char** names, double* ms, doubl
     tms[e.name] += t;
     tb[e.name] += e.bytes;
     cnt[e.name] += 1;
-  }
-  // phases of the persistent decode step (time between grid barriers as seen
-  // by CTA 0, i.e. the slowest CTA), summed over layers
-  if (ctx->mk_traced && ctx->mk_ts) {
-    const int L = ctx->cfg.layers;
-    std::vector<unsigned long long> ts(5 * L + 2);
-    if (cudaMemcpy(ts.data(), ctx->mk_ts, ts.size() * 8, cudaMemcpyDeviceToHost) == cudaSuccess) {
-      const char* nm[5] = {"phase:norm+qkv", "phase:attention", "phase:o", "phase:norm+gateup", "phase:down"};
-      const int H = ctx->H, nqkv = ctx->qd + 2 * ctx->kvd;
-      const double by[5] = {(double)L * nqkv * q8_row_bytes(H), ctx->mk_kv_bytes,
-                            (double)L * H * q8_row_bytes(ctx->qd), 2.0 * L * ctx->F * q8_row_bytes(H),
-                            (double)L * H * q8_row_bytes(ctx->F)};
-      for (int i = 0; i < 5; ++i) {
-        double t = 0;
-        for (int l = 0; l < L; ++l) t += (double)(ts[5 * l + i + 1] - ts[5 * l + i]) * 1e-6;
-        order.push_back(nm[i]);
-        tms[nm[i]] = t;
-        tb[nm[i]] = by[i];
-        cnt[nm[i]] = 0;
-      }
-      std::vector<unsigned long long> t2(4 * (5 * L + 1));
-      if (ctx->mk_ts2 && cudaMemcpy(t2.data(), ctx->mk_ts2, t2.size() * 8, cudaMemcpyDeviceToHost) == cudaSuccess) {
-        // CTA 0's own timeline inside each phase kind: start -> j0 -> j1 -> j2 -> barrier done
-        const char* sub[4] = {"a", "b", "c", "wait"};
-        for (int i = 0; i < 5; ++i) {
-          double acc4[4] = {0, 0, 0, 0};
-          for (int l = 0; l < L; ++l) {
-            const int ph = 5 * l + i;
-            const unsigned long long st0 = ts[ph], m0 = t2[4 * ph], m1 = t2[4 * ph + 1], m2 = t2[4 * ph + 2],
-                                     en = ts[ph + 1];
-            acc4[0] += (double)(m0 - st0) * 1e-6;
-            acc4[1] += (double)(m1 - m0) * 1e-6;
-            acc4[2] += (double)(m2 - m1) * 1e-6;
-            acc4[3] += (double)(en - m2) * 1e-6;
-          }
-          for (int j = 0; j < 4; ++j) {
-            const std::string nmj = std::string("sub:") + (nm[i] + 6) + "." + sub[j];
-            order.push_back(nmj);
-            tms[nmj] = acc4[j];
-            tb[nmj] = 0;
-            cnt[nmj] = 0;
-          }
-        }
-      } else {
-        cudaGetLastError();
-      }
-      order.push_back("phase:norm+lmhead");
-      tms["phase:norm+lmhead"] = (double)(ts[5 * L + 1] - ts[5 * L]) * 1e-6;
-      tb["phase:norm+lmhead"] = (double)ctx->V * q8_row_bytes(H);
-      cnt["phase:norm+lmhead"] = 0;
-    } else {
-      cudaGetLastError();
-    }
   }
   int k = 0;
   static thread_local std::vector<std::string> keep;

@@ -188,6 +188,11 @@ PRESETS: Dict[str, Config] = {
                                 "llama3", 8.0, 1.0, 4.0, 8192.0, False, False),
     "tiny-qwen3": Config("tiny-qwen3", 256, 2, 4, 2, 128, 768, 1200, 1e-6, 1000000.0,
                          "default", 1.0, 1.0, 4.0, 8192.0, True, True),
+    # small shapes the one-launch decode step takes (widths multiples of 512)
+    "small-llama": Config("small-llama", 1024, 3, 16, 4, 64, 2048, 2048, 1e-5, 500000.0,
+                          "llama3", 32.0, 1.0, 4.0, 8192.0, False, True),
+    "small-qwen3": Config("small-qwen3", 1024, 2, 8, 2, 128, 1536, 3072, 1e-6, 1000000.0,
+                          "default", 1.0, 1.0, 4.0, 8192.0, True, False),
 }
 
 

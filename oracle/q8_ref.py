@@ -138,3 +138,83 @@ def time_decode_sample(cfg, batch: int, ctx: int, sample_layers: int = 2, steps:
             "steps": steps,
             "sample": f"{ls} of {cfg.layers} full-width layers + lm_head per token at ctx {ctx}, "
                       f"{steps} timed steps x batch {batch}; layer time scaled by {cfg.layers}/{ls}"}
+
+
+class RefModel:
+    """Whole-model forward on the C restatement (q8r_embed, q8r_layer,
+    q8r_rmsnorm, q8r_gemv): the reference model shell's loop
+    (qwen3_mojo/src/qwen_q8.mojo:126-162) one token at a time, each token
+    through run_layer_q8 at s == 1 (src/llama_q8.mojo:144-230) with an f32 KV
+    cache per layer, then the final norm and the Q8 lm_head
+    (qwen_q8.mojo:141-156).  The checker of the full-size parity tests: all
+    host threads, int8 codes read directly, no dequantized copy of the
+    weights.  ``tensors`` maps checkpoint names to packed rows (uint8 or the
+    uint16 bits of quantize.py's F16 tensor) for 2-D weights and bf16 bits for
+    norm vectors; ``inv`` is the RoPE inverse-frequency table."""
+
+    def __init__(self, cfg, tensors, inv, maxlen: int):
+        self.cfg = cfg
+        L = lib()
+        self._L = L
+        H, QD, KVD, F = cfg.hidden, cfg.q_dim, cfg.kv_dim, cfg.inter
+        u8 = lambda a: np.ascontiguousarray(a).view(np.uint8)
+        u16 = lambda a: np.ascontiguousarray(a).view(np.uint16)
+        self._keep = []
+        self.layers = []
+        for i in range(cfg.layers):
+            p = f"model.layers.{i}."
+            qkv = np.concatenate([u8(tensors[p + f"self_attn.{n}_proj.weight"]) for n in "qkv"], 0)
+            gu = np.concatenate([u8(tensors[p + f"mlp.{n}_proj.weight"]) for n in ("gate", "up")], 0)
+            o, down = u8(tensors[p + "self_attn.o_proj.weight"]), u8(tensors[p + "mlp.down_proj.weight"])
+            inn, post = u16(tensors[p + "input_layernorm.weight"]), u16(tensors[p + "post_attention_layernorm.weight"])
+            qn = u16(tensors[p + "self_attn.q_norm.weight"]) if cfg.qk_norm else None
+            kn = u16(tensors[p + "self_attn.k_norm.weight"]) if cfg.qk_norm else None
+            self._keep += [qkv, gu, o, down, inn, post, qn, kn]
+            self.layers.append(LayerW(qkv.ctypes.data, o.ctypes.data, gu.ctypes.data, down.ctypes.data,
+                                      inn.ctypes.data, post.ctypes.data,
+                                      qn.ctypes.data if qn is not None else None,
+                                      kn.ctypes.data if kn is not None else None))
+        self.embed = u8(tensors["model.embed_tokens.weight"])
+        self.head = self.embed if cfg.tied else u8(tensors["lm_head.weight"])
+        self.fnorm = u16(tensors["model.norm.weight"])
+        self.inv = np.ascontiguousarray(inv, np.float32)
+        self.maxlen = maxlen
+        self.kc = [np.zeros((maxlen, KVD), np.float32) for _ in range(cfg.layers)]
+        self.vc = [np.zeros((maxlen, KVD), np.float32) for _ in range(cfg.layers)]
+        self.scratch = np.zeros(2 * H + 2 * QD + 2 * KVD + 2 * F + 64, np.float32)
+        self.n_cached = 0
+
+    def token(self, tok: int, keep=(), logits: bool = True):
+        """Logits after one token at position n_cached (None when ``logits``
+        is False); ``keep`` lists layers whose output residual is returned too
+        ({layer: h})."""
+        c, L = self.cfg, self._L
+        if self.n_cached >= self.maxlen:
+            raise RuntimeError("KV cache full")
+        h = np.zeros(c.hidden, np.float32)
+        ids = np.array([tok], np.int32)
+        L.q8r_embed(_p(self.embed), c.hidden, _p(ids), 1, _p(h))
+        kept = {}
+        for i in range(c.layers):
+            L.q8r_layer(C.byref(self.layers[i]), _p(h), c.hidden, c.n_heads, c.n_kv, c.head_dim, c.inter, c.eps,
+                        self.n_cached, _p(self.inv), _p(self.kc[i]), _p(self.vc[i]), _p(self.scratch))
+            if i in keep:
+                kept[i] = h.copy()
+        self.n_cached += 1
+        if not logits:
+            return (None, kept) if keep else None
+        xn = np.zeros(c.hidden, np.float32)
+        L.q8r_rmsnorm(_p(h), _p(self.fnorm), 1, c.hidden, c.eps, _p(xn))
+        logits = np.zeros(self.head.shape[0], np.float32)
+        L.q8r_gemv(_p(xn), 1, c.hidden, _p(self.head), self.head.shape[0], _p(logits))
+        return (logits, kept) if keep else logits
+
+    def prefill(self, ids, keep=()):
+        """Logits of the last token and {layer: [len(ids), H]} residuals."""
+        rows = {i: [] for i in keep}
+        lg = None
+        for n, t in enumerate(ids):
+            lg, kept = self.token(int(t), keep=tuple(keep) or (-1,), logits=n == len(ids) - 1)
+            for i in keep:
+                rows[i].append(kept[i])
+        return lg, {i: np.stack(v) for i, v in rows.items()}

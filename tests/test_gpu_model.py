@@ -298,34 +298,48 @@ def test_prefill_attention_context_splits(cuda, cfgname):
     m.close()
 
 
-@pytest.mark.parametrize("cfgname", ["tiny-llama", "tiny-qwen3", "tiny-llama-untied"])
-def test_persistent_decode_step_matches_per_op(cuda, cfgname, monkeypatch):
-    """The opt-in persistent decode step (one cooperative launch per step,
-    Q8_MK=1) against the per-op kernels on the same checkpoint: cached decode
-    logits, on-device generation and batched decode agree with the oracle
-    and with each other."""
+@pytest.mark.parametrize("cfgname", ["small-llama", "small-qwen3", "tiny-llama-untied"])
+def test_ring_decode_step_matches_per_op(cuda, cfgname, monkeypatch):
+    """The one-launch weight-ring decode step (default for one-sequence greedy
+    decode) against the per-operation kernels (Q8_RING=0) on the same
+    checkpoint: cached decode logits match the oracle and each other, and
+    on-device generation, per-step decode and batched decode give the same
+    tokens.  The context grows past several 16-position blocks so that the
+    attention splits and the KV append of the ring step are exercised."""
     ocfg = O.PRESETS[cfgname]
     ck = O.make_q8_checkpoint(ocfg)
-    ids = O.random_ids(ocfg, 11, seed=21)
+    ids = O.random_ids(ocfg, 45, seed=21)
     out = {}
-    for mk in ("0", "1"):
-        monkeypatch.setenv("Q8_MK", mk)
-        m = build(cfgname, maxlen=40, max_seqs=2)
+    for ring in ("0", "1"):
+        monkeypatch.setenv("Q8_RING", ring)
+        m = build(cfgname, maxlen=96, max_seqs=2)
+        m.set_profiling(True)
         m.forward(ids[:-1])
         lg = m.forward([ids[-1]])
+        assert ("decode_step" in m.profile()) == (ring == "1"), m.profile().keys()
+        m.set_profiling(False)
         t = int(np.argmax(lg))
-        gen = m.generate([t], [0], 4)[:, 0].tolist()
+        gen = m.generate([t], [0], 6)[:, 0].tolist()
+        steps = [int(m.decode([gen[-1]], [0])[0])]
+        for _ in range(3):
+            steps.append(int(m.decode([steps[-1]], [0])[0]))
         m.forward(ids[:5], seq=1)
         am, lgb = m.decode([3, 5], [0, 1], logits=True)
-        out[mk] = (lg, gen, lgb)
+        out[ring] = (lg, gen, steps, lgb)
         m.close()
     o = O.OracleModel(ocfg, ck)
     o.forward(ids[:-1])
-    close(out["1"][0], o.forward([ids[-1]]))
+    ref = o.forward([ids[-1]])
+    close(out["1"][0], ref)
+    want = [int(np.argmax(ref))]
+    for _ in range(10):
+        want.append(o.forward_argmax([want[-1]]))
+    assert out["1"][1] == want[1:7]
+    assert out["1"][2] == want[7:11]
     r = O.rel_l2(out["1"][0], out["0"][0])
     assert r < 1e-5, r
-    assert out["1"][1] == out["0"][1]
-    assert O.rel_l2(out["1"][2], out["0"][2]) < 1e-5
+    assert out["1"][1] == out["0"][1] and out["1"][2] == out["0"][2]
+    assert O.rel_l2(out["1"][3], out["0"][3]) < 1e-5
 
 
 def test_batched_decode_matches_single_sequence_wide(cuda):

@@ -153,3 +153,29 @@ def test_sample_c_restatement_matches_literal():
                     assert got == want or margin < 1e-6, (temp, top_p, u, got, want, margin)
                     checked += got == want
     assert checked > 0.99 * 5 * 5 * 3 * 4
+
+
+@pytest.mark.parametrize("cfgname", ["tiny-llama", "tiny-qwen3", "tiny-llama-untied"])
+def test_c_whole_model_matches_pinned_oracle(cfgname):
+    """The C restatement's whole-model loop (oracle.q8_ref.RefModel, the
+    checker of the full-size GPU parity tests) against the numpy oracle,
+    which is pinned to the reference's own gen_oracle / bench_python output:
+    per-layer residuals, last logits and greedy tokens of a cached decode."""
+    from oracle import q8_ref as R
+    cfg = O.PRESETS[cfgname]
+    ck = O.make_q8_checkpoint(cfg)
+    ids = O.random_ids(cfg, 13, seed=5)
+    orc = O.OracleModel(cfg, ck)
+    ref_lg = orc.forward(ids)
+    ref_h = {i: orc.trace[f"after_layer{i}"] for i in (0, 1)}
+    rm = R.RefModel(cfg, ck, O.inv_freq(cfg), maxlen=32)
+    lg, hid = rm.prefill(ids, keep=(0, 1))
+    for i in (0, 1):
+        assert O.rel_l2(hid[i], ref_h[i]) < 1e-5
+    assert O.rel_l2(lg, ref_lg) < 1e-5 and np.abs(lg - ref_lg).max() < 1e-4
+    t_ref, t_c = int(np.argmax(ref_lg)), int(np.argmax(lg))
+    assert t_ref == t_c
+    for _ in range(4):
+        t_ref = orc.forward_argmax([t_ref])
+        t_c = int(np.argmax(rm.token(t_c)))
+        assert t_ref == t_c

@@ -53,8 +53,10 @@ def test_noalloc_gemm_matches_gemm_and_oracle_twice(cuda, M, K, N, dt):
         torch.cuda.synchronize()
         a = y_new.cpu().numpy()
         assert np.isfinite(a).all()
-        assert O.rel_l2(a, b) <= 1e-5 and np.abs(a - b).max() <= 1e-4, (M, K, N)
-        assert O.rel_l2(a, want) <= 1e-5 and np.abs(a - want).max() <= 1e-4, (M, K, N)
+        # q8op_gemm takes the tensor-core GEMM from M = 128 (a different
+        # accumulation order): the kernel tests' GEMM tolerance
+        assert O.rel_l2(a, b) <= 1e-4 and np.abs(a - b).max() <= 1e-3, (M, K, N)
+        assert O.rel_l2(a, want) <= 1e-4 and np.abs(a - want).max() <= 1e-3, (M, K, N)
 
 
 def test_noalloc_gemm_rejects_oversize(cuda):
