@@ -48,7 +48,10 @@ def parse():
     ap.add_argument("--ctx", type=int, default=4096, help="KV capacity per sequence")
     ap.add_argument("--model", default="llama-3.1-8b")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU baseline sample")
+    ap.add_argument("--cpu-layers", type=int, default=0, help="layers in the CPU baseline (0: all)")
+    ap.add_argument("--batches", default="8,64",
+                    help="extra decode batch sizes reported beside the headline batch ('' for none)")
+    ap.add_argument("--extra-steps", type=int, default=32, help="timed steps of each extra batch")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=32)
     return ap.parse_args()
@@ -155,6 +158,49 @@ def run_reference_arm(a):
 
 
 # ----------------------------------------------------------------------------- GPU arm
+def tp_parity(world, rank, local, dist):
+    """Tensor-parallel parity before the timed region: a small model whose
+    heads and vocabulary split over 8 ranks ("tiny-tp8": 8 kv heads, untied
+    vocabulary-parallel head) runs at TP = world (NCCL prefill, the P2P decode
+    exchange) and, on rank 0's GPU, at TP = 1 with the same GPU-made weights.
+    The single-GPU path is the one the parity tests pin to the oracle.
+    Returns (rank 0) the relative L2 of the layer-1 residual and the last
+    prefill logits, and whether 8 greedy tokens agree."""
+    import numpy as np
+
+    from lama32_mojo_b200.config import PRESETS
+    from lama32_mojo_b200.model import load_synthetic, nccl_unique_id
+
+    tcfg = PRESETS["tiny-tp8"]
+    uid = [nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    ids = np.random.default_rng(7).integers(0, tcfg.vocab, size=12).tolist()
+
+    def run(mod):
+        h1 = mod.forward_hidden(ids, 1)
+        lg = mod.forward(ids)
+        toks = [int(np.argmax(lg))]
+        for _ in range(7):
+            toks.append(int(mod.decode([toks[-1]], [0])[0]))
+        mod.close()
+        return h1, lg, toks
+
+    got = run(load_synthetic(tcfg, device=local, seed=5, maxlen=64, max_seqs=1, tp_rank=rank, tp_size=world,
+                             nccl_id=uid[0]))
+    out = None
+    if rank == 0:
+        ref = run(load_synthetic(tcfg, device=local, seed=5, maxlen=64, max_seqs=1))
+        rl2 = lambda x, y: float(np.linalg.norm(np.asarray(x, np.float64) - y) / max(np.linalg.norm(y), 1e-30))
+        out = {"config": "tiny-tp8 (hidden 512, 2 layers, 8/8 heads, vocab 2048 untied)", "tp": world,
+               "reference": "TP=1 on rank 0 (the oracle-pinned single-GPU path), same weights",
+               "rel_l2_hidden_layer1": rl2(got[0], ref[0]), "rel_l2_logits": rl2(got[1], ref[1]),
+               "tokens_equal": got[2] == ref[2], "tokens": got[2]}
+        out["pass"] = bool(out["rel_l2_hidden_layer1"] <= 1e-5 and out["rel_l2_logits"] <= 1e-5
+                           and out["tokens_equal"])
+    dist.barrier()
+    return out
+
+
 def main():
     a = parse()
     if a.impl == "reference":
@@ -184,9 +230,11 @@ def main():
 
     cfg = PRESETS[a.model]
     B = a.batch
+    batches = [int(v) for v in a.batches.split(",") if v.strip()] if a.batches else []
     prompt, ctx_mid, config = workload(a, world)
     assert prompt > 0, "ctx too small for warmup+steps"
-    m = load_synthetic(cfg, device=local, seed=0, maxlen=a.ctx, max_seqs=B, max_tokens=2048,
+    tpp = tp_parity(world, rank, local, dist) if world > 1 else None
+    m = load_synthetic(cfg, device=local, seed=0, maxlen=a.ctx, max_seqs=max([B] + batches), max_tokens=2048,
                        tp_rank=rank, tp_size=world, nccl_id=nid)
     rng = np.random.default_rng(1)
     first = []
@@ -280,7 +328,8 @@ def main():
     g_l = sum(agg[k][2] for k in dom)
     peak, peak_kind = load_peaks()
     achieved = g_b / (g_ms / 1e3) / 1e9 if g_ms > 0 else 0.0
-    step_ms_prof = sum(v[0] for v in agg.values()) / nprof
+    # "phase:*" entries split the ring step's time (no launches of their own)
+    step_ms_prof = sum(v[0] for k, v in agg.items() if not k.startswith("phase:")) / nprof
     breakdown = {k: {"ms_per_step": round(v[0] / nprof, 4), "launches_per_step": v[2] // nprof,
                      "GB_s": round(v[1] / (v[0] / 1e3) / 1e9, 1) if v[0] > 0 else None} for k, v in agg.items()}
     traffic = None
@@ -290,8 +339,9 @@ def main():
         traffic = tj.get(f"{a.model}/tp{world}/b{B}")
 
     # launches per step: our kernels inside the generate graph = the profiled
-    # decode launches + the on-device step epilogue (k_step_end)
-    launches_per_step = sum(v[2] for v in agg.values()) // nprof + 1
+    # decode launches + the on-device step epilogue (k_step_end), which the
+    # one-launch ring step does itself
+    launches_per_step = sum(v[2] for v in agg.values()) // nprof + (0 if "decode_step" in agg else 1)
     gpu_launches = launches_per_step * a.steps
 
     # prefill summary: algorithmic GEMM flops (2*M*N*K; the split-operand mode
@@ -316,6 +366,43 @@ def main():
                "share": {k: round(v[0] / tot_ms, 3) for k, v in pprof.items()} if tot_ms > 0 else None}
 
     step_bytes = cfg.decode_bytes(B, ctx_mid, tp=world)
+    peak_bw = load_peaks()[0]
+
+    # ---- the other config[3] batch sizes: fresh prompts, device-resident loop
+    extra = {}
+    for Bx in batches:
+        xs = list(range(Bx))
+        xprompt = a.ctx - a.warmup - a.extra_steps - 8
+        firsts = []
+        for s in xs:
+            m.reset(s)
+            lg = m.forward(rng.integers(0, cfg.vocab, size=xprompt).tolist(), seq=s)
+            firsts.append(int(np.argmax(lg)))
+        cur_x = m.generate(firsts, xs, a.warmup)[-1].tolist()
+        barrier()
+        torch.cuda.synchronize()
+        x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        x0.record(ext)
+        tx = m.generate(cur_x, xs, a.extra_steps)
+        x1.record(ext)
+        torch.cuda.synchronize()
+        barrier()
+        xms = x0.elapsed_time(x1)
+        if world > 1:
+            t = torch.tensor([xms], dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            xms = float(t.item())
+        if tx.min() < 0 or tx.max() >= cfg.vocab:
+            raise SystemExit("decode produced out-of-range tokens: the workload is invalid")
+        xmid = xprompt + a.warmup + a.extra_steps // 2
+        xb = cfg.decode_bytes(Bx, xmid, tp=world)
+        xstep = xms / a.extra_steps
+        extra[str(Bx)] = {"value": round(Bx * a.extra_steps / (xms / 1e3), 2), "unit": "tok/s",
+                          "ms_per_step": round(xstep, 4), "steps": a.extra_steps,
+                          "context": f"{xprompt}..{xprompt + a.warmup + a.extra_steps}",
+                          "step_roofline": {"bytes_per_step": xb,
+                                            "achieved_GB_s": round(xb / (xstep / 1e3) / 1e9, 1),
+                                            "frac": round(xb / (xstep / 1e3) / 1e9 / peak_bw, 4)}}
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu:
@@ -345,7 +432,10 @@ def main():
             "gpu_launches": gpu_launches, "clocks": clk.summary(),
             "cpu_baseline": cpu,
             "prefill": prefill,
+            "batches": extra,
         }
+        if tpp is not None:
+            line["tp_parity"] = tpp
         print(json.dumps(line), flush=True)
     m.close()
     if world > 1:

@@ -23,17 +23,19 @@
 //   * 8 consumer warps that wait for the previous phase of the whole grid
 //     (a monotonic arrival counter), stage the phase's activation vector once
 //     per CTA, and drain the ring.
-// The producer therefore runs up to a ring's worth of bytes (136 KB per SM)
+// The producer therefore runs up to a ring's worth of bytes (128 KB per SM)
 // ahead across phase and layer boundaries, and HBM keeps streaming while the
 // grid synchronizes.
 //
 // Ring.  Consumer warp w owns slots 2w and 2w+1 (full / empty mbarrier pair
 // each) and takes its items in order, alternating slots; the producer fills
 // them in the same order, so no wait ever targets a phase more than one
-// ahead.  A GEMV stage is 16 weight rows x 512 codes (rows padded to 528 B in
-// shared memory so that ldmatrix is conflict-free) plus their 16 x 8 f16
-// group scales; an attention block is 16 K rows (padded) in one slot and 16
-// V rows in the other.
+// ahead.  A GEMV stage is 16 weight rows x 512 codes, four tensor-map boxes
+// of 16 x 128 B with the 128 B swizzle (16-byte chunk c of row r stored at c ^
+// (r & 7), so ldmatrix is conflict-free), plus one box of their 16 x 8 f16
+// group scales: five copies per 8.25 KB; an attention block is 16 K rows
+// (tensor-map boxes of 16 x 32 floats, same swizzle) in one slot and 16 V rows
+// (one bulk copy) in the other.
 //
 // GEMV arithmetic (as the standalone digit GEMV): int8 codes straight to
 // mma.m16n8k32.s8 against the activations written as three int8 digits per
@@ -124,13 +126,11 @@ __device__ __forceinline__ void dr_grid_wait(const DrParams& P, unsigned int tar
   dr_csync();
 }
 
-// Every consumer thread's stores of the phase, then one gpu-scope release.
+// Every consumer thread's stores of the phase (ordered before thread 0 by the
+// CTA barrier), then one gpu-scope release increment.
 __device__ __forceinline__ void dr_grid_arrive(const DrParams& P) {
   dr_csync();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(P.bar, 1u);
-  }
+  if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(P.bar) : "memory");
 }
 
 __device__ __forceinline__ void dr_ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -147,14 +147,31 @@ __device__ __forceinline__ void dr_imma(int (&d)[4], uint32_t a0, uint32_t a1, u
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// CTA 0's phase timeline (profiling): globaltimer into trace[ph * 4 + j].
+__device__ __forceinline__ void dr_mark(const DrParams& P, int ph, int j) {
+  if (P.trace && blockIdx.x == 0 && threadIdx.x == 0) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    P.trace[ph * 4 + j] = t;
+  }
+}
+
 // ------------------------------------------------------------------ phases
 // Phase ph of the step: layer ph / 5, kind ph % 5; the last phase is lm_head.
 __device__ __forceinline__ int dr_kind(const DrParams& P, int ph) { return ph == 5 * P.L ? DP_LM : ph % 5; }
 
+// CTAs a split phase of S stages (C per tile) spreads over: at most G, and
+// few enough that every range holds at least ceil(C / 2) stages, so that a
+// tile meets at most 3 ranges.
+__host__ __device__ __forceinline__ int dr_split_ctas(long long S, int C, int G) {
+  const long long per = (C + 1) / 2;
+  const long long g = S / per;
+  return (int)(g < G ? (g < 1 ? 1 : g) : G);
+}
+
 // One GEMV phase as one CTA sees it.
 struct DrG {
-  const uint8_t* W;
-  int64_t rb;
+  const uint8_t* W;  // the matrix in ring layout (block st at W + st * DR_BLOCK)
   int K, C, T;   // inputs, 512-code chunks per row, 16-row tiles
   int F2;        // SwiGLU: rows of tile t are gate t*8.. and up F2 + t*8..; 0: rows t*16..
   int s0, s1;    // this CTA's stages [s0, s1) of T*C
@@ -176,11 +193,10 @@ __device__ __forceinline__ DrG dr_gemv_desc(const DrParams& P, int kind, int L) 
   }
   d.T = d.F2 ? N / 8 : N / 16;
   d.C = d.K / DR_CK;
-  d.rb = (int64_t)d.K + d.K / 32;
   const int G = gridDim.x, c = blockIdx.x;
-  if (d.split) {  // over the first min(G, S) CTAs, so that every range holds a stage
+  if (d.split) {  // over the first dr_split_ctas CTAs: each range holds >= C/2 stages
     const long long S = (long long)d.T * d.C;
-    const int Gs = (int)min((long long)G, S);
+    const int Gs = dr_split_ctas(S, d.C, G);
     d.s0 = c < Gs ? (int)(S * c / Gs) : (int)S;
     d.s1 = c < Gs ? (int)(S * (c + 1) / Gs) : (int)S;
   } else {
@@ -190,35 +206,20 @@ __device__ __forceinline__ DrG dr_gemv_desc(const DrParams& P, int kind, int L) 
   return d;
 }
 
-// CTA whose split range holds stage x: the largest c with floor(c S / Gs) <=
-// x, Gs = min(G, S) (every one of those ranges is non-empty).
-__device__ __forceinline__ int dr_cta_of(long long x, long long S) {
-  const long long Gs = min((long long)gridDim.x, S);
+// CTA whose split range holds stage x: the largest c with floor(c S / Gs) <= x.
+__device__ __forceinline__ int dr_cta_of(long long x, long long S, int C) {
+  const long long Gs = dr_split_ctas(S, C, gridDim.x);
   return (int)(((x + 1) * Gs - 1) / S);
 }
 
-// Partial slots of down-projection tile t (rows t*16 .. t*16+15): one per
-// CTA whose range meets the tile, in CTA order.
-__device__ __forceinline__ int dr_down_slots(const DrParams& P, int t) {
-  const int C = P.F / DR_CK;
-  const long long S = (long long)(P.H / 16) * C;
-  return dr_cta_of((long long)(t + 1) * C - 1, S) - dr_cta_of((long long)t * C, S) + 1;
-}
-
 // ------------------------------------------------------------------ producer
-__device__ __forceinline__ void dr_issue_stage(const DrParams& P, const DrG& d, int st, uint8_t* ring, uint64_t* full,
-                                               uint64_t* empty, int slot, int use, int lane) {
+__device__ __forceinline__ void dr_issue_stage(const DrParams& P, const DrG& d, int st, uint8_t* ring,
+                                               uint64_t* full, uint64_t* empty, int slot, int use, int lane) {
   if (use > 0) dr_mwait(&empty[slot], (uint32_t)((use - 1) & 1), P.status);
-  uint8_t* dst = ring + slot * DR_SLOT_BYTES;
-  const int t = st / d.C, ch = st % d.C;
-  if (lane == 0) mbar_arrive_expect_tx(&full[slot], 16 * DR_CK + 16 * 16);
-  __syncwarp();
-  const int r = lane & 15;
-  const int64_t row = d.F2 ? (r < 8 ? (int64_t)t * 8 + r : (int64_t)d.F2 + (int64_t)t * 8 + (r - 8))
-                           : (int64_t)t * 16 + r;
-  const uint8_t* src = d.W + row * d.rb;
-  if (lane < 16) bulk_g2s(dst + r * DR_RS, src + d.K / 32 + (int64_t)ch * DR_CK, DR_CK, &full[slot]);
-  else bulk_g2s(dst + 16 * DR_RS + r * 16, src + (int64_t)ch * 16, 16, &full[slot]);
+  if (lane == 0) {
+    mbar_arrive_expect_tx(&full[slot], DR_BLOCK);
+    bulk_g2s(ring + slot * DR_SLOT_BYTES, d.W + (int64_t)st * DR_BLOCK, DR_BLOCK, &full[slot]);
+  }
 }
 
 template <int HD>
@@ -244,15 +245,13 @@ __device__ __forceinline__ void dr_produce_attn(const DrParams& P, int L, uint8_
         if (uv > 0) dr_mwait(&empty[sv], (uint32_t)((uv - 1) & 1), P.status);
         const int key0 = (bl0 + i) * 16;
         const int64_t row0 = ((int64_t)btr[key0 / P.page] * P.nkv + kvh) * P.page + (key0 % P.page);
+        // 16 consecutive rows of one page: one bulk copy each for K and V
         if (lane == 0) {
           mbar_arrive_expect_tx(&full[sk], 16 * HD * 4);
+          bulk_g2s(ring + sk * DR_SLOT_BYTES, kp + row0 * HD, 16 * HD * 4, &full[sk]);
           mbar_arrive_expect_tx(&full[sv], 16 * HD * 4);
-        }
-        __syncwarp();
-        if (lane < 16)
-          bulk_g2s(ring + sk * DR_SLOT_BYTES + lane * (HD * 4 + 16), kp + (row0 + lane) * HD, HD * 4, &full[sk]);
-        else if (lane == 16)
           bulk_g2s(ring + sv * DR_SLOT_BYTES, vp + row0 * HD, 16 * HD * 4, &full[sv]);
+        }
         u[w] += 2;
       }
     }
@@ -343,9 +342,11 @@ __device__ __forceinline__ void dr_digits16(const float (&v)[16], bool valid, in
 
 enum { DS_F32 = 0, DS_EMBED = 1, DS_FOLD = 2 };
 
-// 16 values x[k0 .. k0+15] of the phase's input vector.
-__device__ __forceinline__ void dr_load16(const DrParams& P, int kind, const float* src, int k0, float (&v)[16]) {
-  if (kind == DS_EMBED) {
+// 16 values x[k0 .. k0+15] of the phase's input vector; every load of the
+// item is in flight before the first is used.
+template <int KIND>
+__device__ __forceinline__ void dr_load16(const DrParams& P, const float* src, int k0, float (&v)[16]) {
+  if constexpr (KIND == DS_EMBED) {
     const int64_t rb = (int64_t)P.H + P.H / 32;
     const uint8_t* row = P.embed + (int64_t)P.ids[0] * rb;
     const float s = __half2float(__ushort_as_half(reinterpret_cast<const unsigned short*>(row)[k0 / 64]));
@@ -355,53 +356,72 @@ __device__ __forceinline__ void dr_load16(const DrParams& P, int kind, const flo
     for (int i = 0; i < 16; ++i) v[i] = (float)(int8_t)((qw[i >> 2] >> (8 * (i & 3))) & 0xFF) * s;
     return;
   }
+  else {
+  float4 a[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float4 a = __ldcg(reinterpret_cast<const float4*>(src + k0) + i);
-    v[4 * i] = a.x; v[4 * i + 1] = a.y; v[4 * i + 2] = a.z; v[4 * i + 3] = a.w;
-  }
-  if (kind == DS_FOLD) {  // residual + the down partial slots of its tile, in slot order
-    const int ns = dr_down_slots(P, k0 / 16);
-    for (int s = 0; s < ns; ++s) {
+  for (int i = 0; i < 4; ++i) a[i] = __ldcg(reinterpret_cast<const float4*>(src + k0) + i);
+  if constexpr (KIND == DS_FOLD) {  // residual + the down partial slots, in slot order
+    float4 pp[DR_NS][4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float4 a = __ldcg(reinterpret_cast<const float4*>(P.pres + (int64_t)s * P.H + k0) + i);
-        v[4 * i] += a.x; v[4 * i + 1] += a.y; v[4 * i + 2] += a.z; v[4 * i + 3] += a.w;
+    for (int sl = 0; sl < DR_NS; ++sl)
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        pp[sl][i] = sl < P.nsf ? __ldcg(reinterpret_cast<const float4*>(P.pres + (int64_t)sl * P.H + k0) + i)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int sl = 0; sl < DR_NS; ++sl) {
+      if (sl < P.nsf) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          a[i].x += pp[sl][i].x; a[i].y += pp[sl][i].y; a[i].z += pp[sl][i].z; a[i].w += pp[sl][i].w;
+        }
       }
     }
   }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[4 * i] = a[i].x; v[4 * i + 1] = a[i].y; v[4 * i + 2] = a[i].z; v[4 * i + 3] = a[i].w;
+  }
+  }
 }
 
-// Stages the K inputs of a GEMV phase as digits: x from `kind`; with nw,
-// x = nw * x / sqrt(mean(x^2) + eps) (K <= 8192); with wb, this CTA's slice
-// of the raw x is written back (the residual of the layer).
-__device__ void dr_stage(const DrParams& P, int K, int kind, const float* src, const uint16_t* nw, float* wb,
-                         uint8_t* xq, float4* fcol, float* scr) {
+// Stages the K inputs of a GEMV phase as digits: waits for the previous
+// phase of the grid (target arrivals; 0: none), then x from `kind`; with nw
+// (K <= 16 x 256), x = nw * x / sqrt(mean(x^2) + eps), the norm weights read
+// before the wait; with wb, this CTA's slice of the raw x is written back
+// (the residual of the layer).
+template <int KIND, bool RMS>
+__device__ void dr_stage(const DrParams& P, int ph, unsigned int target, int K, const float* src,
+                         const uint16_t* nw, float* wb, uint8_t* xq, float4* fcol, float* scr) {
   constexpr int NT = DR_CW * 32;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, sq = lane & 3;
   const int nitem = K / 16;  // quarter-groups
-  if (nw) {
-    float v[2][16];
+  if constexpr (RMS) {
+    const bool valid = tid < nitem;
+    const int k0 = tid * 16;
+    uint4 w0 = make_uint4(0, 0, 0, 0), w1 = w0;
+    if (valid) {
+      w0 = __ldg(reinterpret_cast<const uint4*>(nw + k0));
+      w1 = __ldg(reinterpret_cast<const uint4*>(nw + k0 + 8));
+    }
+    if (target) dr_grid_wait(P, target);
+    dr_mark(P, ph, 0);
+    float v[16];
     float ss = 0.f;
+    if (valid) {
+      dr_load16<KIND>(P, src, k0, v);
 #pragma unroll
-    for (int it = 0; it < 2; ++it) {
-      const int item = it * NT + tid;
-      if (item < nitem) {
-        const int k0 = item * 16;
-        dr_load16(P, kind, src, k0, v[it]);
+      for (int i = 0; i < 16; ++i) ss = fmaf(v[i], v[i], ss);
+      if (wb) {
+        const int G = gridDim.x, c = blockIdx.x;
+        const int s0 = (int)((long long)K * c / G), s1 = (int)((long long)K * (c + 1) / G);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) ss = fmaf(v[it][i], v[it][i], ss);
-        if (wb) {
-          const int G = gridDim.x, c = blockIdx.x;
-          const int w0 = (int)((long long)K * c / G), w1 = (int)((long long)K * (c + 1) / G);
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            if (k0 + i >= w0 && k0 + i < w1) wb[k0 + i] = v[it][i];
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[it][i] = 0.f;
+        for (int i = 0; i < 16; ++i)
+          if (k0 + i >= s0 && k0 + i < s1) wb[k0 + i] = v[i];
       }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = 0.f;
     }
     ss = warp_sum(ss);
     if (lane == 0) scr[warp] = ss;
@@ -410,35 +430,38 @@ __device__ void dr_stage(const DrParams& P, int K, int kind, const float* src, c
 #pragma unroll
     for (int w = 0; w < DR_CW; ++w) tot += scr[w];
     const float inv = 1.0f / sqrtf(tot / (float)K + P.eps);
+    if (valid) {
+      const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-    for (int it = 0; it < 2; ++it) {
-      const int item = it * NT + tid;
-      const bool valid = item < nitem;
-      if (valid) {
-        const int k0 = item * 16;
-        const uint4 w0 = __ldg(reinterpret_cast<const uint4*>(nw + k0));
-        const uint4 w1 = __ldg(reinterpret_cast<const uint4*>(nw + k0 + 8));
-        const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      for (int i = 0; i < 8; ++i) {
+        v[2 * i] = __uint_as_float(ww[i] << 16) * v[2 * i] * inv;
+        v[2 * i + 1] = __uint_as_float(ww[i] & 0xFFFF0000u) * v[2 * i + 1] * inv;
+      }
+    }
+    dr_digits16(v, valid, valid ? tid >> 2 : 0, sq, xq, fcol);
+  } else {
+    if (target) dr_grid_wait(P, target);
+    dr_mark(P, ph, 0);
+    constexpr int R = 2;  // rounds whose loads are in flight together
+    for (int base = 0; base < nitem; base += R * NT) {
+      float v[R][16];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          v[it][2 * i] = __uint_as_float(ww[i] << 16) * v[it][2 * i] * inv;
-          v[it][2 * i + 1] = __uint_as_float(ww[i] & 0xFFFF0000u) * v[it][2 * i + 1] * inv;
+      for (int r = 0; r < R; ++r) {
+        const int item = base + r * NT + tid;
+        if (item < nitem) dr_load16<KIND>(P, src, item * 16, v[r]);
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int item = base + r * NT + tid;
+        if (base + r * NT < nitem) {
+          const bool valid = item < nitem;
+          if (!valid) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[r][i] = 0.f;
+          }
+          dr_digits16(v[r], valid, valid ? item >> 2 : 0, sq, xq, fcol);
         }
       }
-      if (it * NT < nitem) dr_digits16(v[it], valid, valid ? item >> 2 : 0, sq, xq, fcol);
-    }
-  } else {
-    for (int base = 0; base < nitem; base += NT) {
-      float v[16];
-      const int item = base + tid;
-      const bool valid = item < nitem;
-      if (valid) {
-        dr_load16(P, kind, src, item * 16, v);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = 0.f;
-      }
-      dr_digits16(v, valid, valid ? item >> 2 : 0, sq, xq, fcol);
     }
   }
   dr_csync();
@@ -460,14 +483,18 @@ __device__ __forceinline__ void dr_flush(float* red, int lt, int warp, int g, in
 // Warp `warp` drains its run of the CTA's stages; per-tile sums into red
 // [local tile][warp][16 rows].
 __device__ __forceinline__ void dr_gemv_run(const DrParams& P, const DrG& d, uint8_t* ring, uint64_t* full,
-                                            uint64_t* empty, const uint8_t* xq, const float4* fcol, float* red,
-                                            int& u, int warp, int lane) {
+                                            uint64_t* empty, const uint8_t* xq, const float4* fcol, float* red, int& u,
+                                            int warp, int lane) {
   const int n = d.s1 - d.s0;
   const int a = d.s0 + (int)((long long)n * warp / DR_CW), b = d.s0 + (int)((long long)n * (warp + 1) / DR_CW);
   const int t_lo = d.s0 / d.C;
   const int g = lane >> 2, t = lane & 3;
+  // ldmatrix x4: lane l addresses row rr + 8 (l >> 3 & 1) of the 16 rows and
+  // 16-byte chunk (l >> 4) of the k32 half; a box row holds 8 chunks stored
+  // at chunk ^ (row & 7) (128 B swizzle)
   const int mat = lane >> 3, rr = lane & 7;
-  const uint32_t lofs = (uint32_t)((rr + 8 * (mat & 1)) * DR_RS + 16 * (mat >> 1));
+  const int lrow = rr + 8 * (mat & 1), mh = mat >> 1;
+  const uint32_t lofs = (uint32_t)(lrow * 128);
   const bool has_col = g < 3;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   int cur = -1;
@@ -482,14 +509,16 @@ __device__ __forceinline__ void dr_gemv_run(const DrParams& P, const DrG& d, uin
     dr_mwait(&full[slot], (uint32_t)((u >> 1) & 1), P.status);
     const uint8_t* sb = ring + slot * DR_SLOT_BYTES;
     const uint32_t sbase = smem_u32(sb) + lofs;
-    const uint4 sA = *reinterpret_cast<const uint4*>(sb + 16 * DR_RS + g * 16);
-    const uint4 sB = *reinterpret_cast<const uint4*>(sb + 16 * DR_RS + (g + 8) * 16);
+    const uint4 sA = *reinterpret_cast<const uint4*>(sb + 16 * DR_CK + g * 16);
+    const uint4 sB = *reinterpret_cast<const uint4*>(sb + 16 * DR_CK + (g + 8) * 16);
 #pragma unroll
     for (int grp = 0; grp < 8; ++grp) {
       const int gi = ch * 8 + grp;
+      const int c0 = 4 * (grp & 1) + mh;
+      const uint32_t bx0 = sbase + (grp >> 1) * 2048;
       uint32_t a0, a1, a2, a3, a4, a5, a6, a7;
-      dr_ldsm_x4(sbase + grp * 64, a0, a1, a2, a3);
-      dr_ldsm_x4(sbase + grp * 64 + 32, a4, a5, a6, a7);
+      dr_ldsm_x4(bx0 + ((c0 ^ rr) << 4), a0, a1, a2, a3);
+      dr_ldsm_x4(bx0 + (((c0 + 2) ^ rr) << 4), a4, a5, a6, a7);
       uint4 bx = make_uint4(0, 0, 0, 0);
       if (has_col) bx = *reinterpret_cast<const uint4*>(xq + (int64_t)gi * 192 + g * 64 + t * 16);
       int dd[4] = {0, 0, 0, 0};
@@ -534,11 +563,12 @@ __device__ __forceinline__ unsigned long long dr_key(float v, int idx) {
 }
 
 // ------------------------------------------------------------------ attention consumer
+
 template <int HD>
 __device__ void dr_attn(const DrParams& P, int L, uint8_t* ring, uint64_t* full, uint64_t* empty, int& u, float* sQ,
                         float* sP, float* sKn, float* sVn, float* sX, float (*sm_m)[DR_GMAX],
                         float (*sm_l)[DR_GMAX], int* s_last) {
-  constexpr int E = HD / 32, CH = HD / 4, J = HD / 32, KR = HD + 4;
+  constexpr int E = HD / 32, CH = HD / 4, J = HD / 32;
   const int c = blockIdx.x, ns = P.nsplit;
   if (c >= P.nkv * ns) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -625,7 +655,7 @@ __device__ void dr_attn(const DrParams& P, int L, uint8_t* ring, uint64_t* full,
     dr_mwait(&full[sv], (uint32_t)(uv & 1), P.status);
     if (own_new && p >= key0 && p < key0 + 16) {  // the appended row, from the prologue
       for (int c4 = lane; c4 < CH; c4 += 32) {
-        *reinterpret_cast<float4*>(kb + (p - key0) * KR + 4 * c4) = *reinterpret_cast<const float4*>(sKn + 4 * c4);
+        *reinterpret_cast<float4*>(kb + (p - key0) * HD + 4 * c4) = *reinterpret_cast<const float4*>(sKn + 4 * c4);
         *reinterpret_cast<float4*>(vb + (p - key0) * HD + 4 * c4) = *reinterpret_cast<const float4*>(sVn + 4 * c4);
       }
       // these generic writes land before the bulk copy that later refills the slots
@@ -640,9 +670,13 @@ __device__ void dr_attn(const DrParams& P, int L, uint8_t* ring, uint64_t* full,
       const float4* q4 = reinterpret_cast<const float4*>(sQ);
 #pragma unroll 2
       for (int cc = 0; cc < CH / 2; cc += 2) {
-        const int c0 = ((cc >> 2) << 3) + hh + (cc & 3), c1 = c0 + 1;  // this lane's half of the chunks
-        const float4 k0 = *reinterpret_cast<const float4*>(kb + jr * KR + 4 * c0);
-        const float4 k1 = *reinterpret_cast<const float4*>(kb + jr * KR + 4 * c1);
+        // this lane's half of the chunks (hh), in an order rotated by the
+        // position: the 4 positions x 2 halves of an 8-lane phase read 8
+        // different bank groups of the plain K rows (and of q)
+        const int grp8 = (cc >> 2) << 3;
+        const int c0 = grp8 + hh + ((cc + jr) & 3), c1 = grp8 + hh + ((cc + 1 + jr) & 3);
+        const float4 k0 = *reinterpret_cast<const float4*>(kb + jr * HD + 4 * c0);
+        const float4 k1 = *reinterpret_cast<const float4*>(kb + jr * HD + 4 * c1);
 #pragma unroll
         for (int g = 0; g < DR_GMAX; ++g) {
           if (g < G) {
@@ -759,7 +793,7 @@ __device__ void dr_attn(const DrParams& P, int L, uint8_t* ring, uint64_t* full,
   dr_csync();
   if (threadIdx.x == 0) {
     int old;
-    asm volatile("fence.acq_rel.gpu;\n\tatom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
                  : "=r"(old)
                  : "l"(P.aticket + kvh)
                  : "memory");
@@ -873,34 +907,41 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P)
   const int nphase = 5 * P.L + 1;
   for (int ph = 0; ph < nphase; ++ph) {
     const int kind = dr_kind(P, ph), L = ph / 5;
-    if (ph > 0) {
-      target += (unsigned int)G;
-      dr_grid_wait(P, target);
-    }
+    if (ph > 0) target += (unsigned int)G;
     if (kind == DP_ATTN) {
+      dr_grid_wait(P, target);
+      dr_mark(P, ph, 0);
       dr_attn<HD>(P, L, ring, full, empty, u, sQ, sP, sKn, sVn, reinterpret_cast<float*>(xq), sm_m, sm_l, &s_last);
+      dr_mark(P, ph, 1);
+      dr_mark(P, ph, 2);
       dr_grid_arrive(P);
+      dr_mark(P, ph, 3);
       continue;
     }
     const DrG d = dr_gemv_desc(P, kind, L);
     const DrLayer* ly = P.layers + (kind == DP_LM ? 0 : L);
     float* hc = (L & 1) ? P.h1 : P.h0;  // this layer's residual
     float* hp = (L & 1) ? P.h0 : P.h1;  // the previous layer's
+    // the stagings wait for the previous phase (after their static loads);
+    // mark 0 is then the end of the wait
     switch (kind) {
       case DP_QKV:
-        dr_stage(P, P.H, L == 0 ? DS_EMBED : DS_FOLD, hp, ly->in_norm, hc, xq, fcol, scr);
+        if (L == 0) dr_stage<DS_EMBED, true>(P, ph, target, P.H, hp, ly->in_norm, hc, xq, fcol, scr);
+        else dr_stage<DS_FOLD, true>(P, ph, target, P.H, hp, ly->in_norm, hc, xq, fcol, scr);
         break;
-      case DP_O: dr_stage(P, P.qd, DS_F32, P.ao, nullptr, nullptr, xq, fcol, scr); break;
-      case DP_GU: dr_stage(P, P.H, DS_F32, hc, ly->post_norm, nullptr, xq, fcol, scr); break;
-      case DP_DOWN: dr_stage(P, P.F, DS_F32, P.act, nullptr, nullptr, xq, fcol, scr); break;
+      case DP_O: dr_stage<DS_F32, false>(P, ph, target, P.qd, P.ao, nullptr, nullptr, xq, fcol, scr); break;
+      case DP_GU: dr_stage<DS_F32, true>(P, ph, target, P.H, hc, ly->post_norm, nullptr, xq, fcol, scr); break;
+      case DP_DOWN: dr_stage<DS_F32, false>(P, ph, target, P.F, P.act, nullptr, nullptr, xq, fcol, scr); break;
       default: {
         const int Lp = P.L - 1;
-        dr_stage(P, P.H, DS_FOLD, (Lp & 1) ? P.h1 : P.h0, P.final_norm, nullptr, xq, fcol, scr);
+        dr_stage<DS_FOLD, true>(P, ph, target, P.H, (Lp & 1) ? P.h1 : P.h0, P.final_norm, nullptr, xq, fcol, scr);
       }
     }
     float* red = reinterpret_cast<float*>(xq + (((size_t)d.K * 3 + 15) & ~(size_t)15));
+    dr_mark(P, ph, 1);
     dr_gemv_run(P, d, ring, full, empty, xq, fcol, red, u, warp, lane);
     dr_csync();
+    dr_mark(P, ph, 2);
 
     // epilogue over the CTA's tiles
     const int n = d.s1 - d.s0;
@@ -935,7 +976,7 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P)
         for (int w = 0; w < DR_CW; ++w) b = s_key[w] > b ? s_key[w] : b;
         if (b) atomicMax(P.amax, b);
         int old;
-        asm volatile("fence.acq_rel.gpu;\n\tatom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
                      : "=r"(old)
                      : "l"(P.lm_ticket)
                      : "memory");
@@ -954,6 +995,7 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P)
           *P.lm_ticket = 0;
         }
       }
+      dr_mark(P, ph, 3);
       continue;  // the last phase: no arrival
     } else {
       for (int i = threadIdx.x; i < ntile * 16; i += NT) {
@@ -964,20 +1006,70 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P)
           P.qkv[row] = v;
         } else if (kind == DP_O) {
           hc[row] = __ldcg(hc + row) + v;
-        } else {  // DP_DOWN: this CTA's partial of the tile into its slot
+        } else {  // DP_DOWN: this CTA's partial of the tile into its slot;
+                  // the tile's last CTA zeroes the slots no CTA fills
           const long long S = (long long)d.T * d.C;
-          const int slot = c - dr_cta_of((long long)tile * d.C, S);
-          P.pres[(int64_t)slot * P.H + row] = v;
+          const int c0 = dr_cta_of((long long)tile * d.C, S, d.C);
+          const int c1 = dr_cta_of((long long)(tile + 1) * d.C - 1, S, d.C);
+          P.pres[(int64_t)(c - c0) * P.H + row] = v;
+          if (c == c1)
+            for (int sl = c1 - c0 + 1; sl < P.nsf; ++sl) P.pres[(int64_t)sl * P.H + row] = 0.f;
         }
       }
     }
     dr_grid_arrive(P);
+    dr_mark(P, ph, 3);
   }
+}
+
+// ------------------------------------------------------------------ ring layout
+// One thread per 16-byte chunk of the output: block (t, c) = 16 rows x 512
+// codes in swizzled boxes, then the rows' 8 group scales of chunk c.
+__global__ void k_ring_pack(const uint8_t* __restrict__ W, int64_t nchunk16, int K, int C, int f2,
+                            uint8_t* __restrict__ dst) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= nchunk16) return;
+  const int64_t blk = e / (DR_BLOCK / 16);
+  const int q = (int)(e % (DR_BLOCK / 16));
+  const int64_t t = blk / C;
+  const int c = (int)(blk % C);
+  const int64_t rb = (int64_t)K + K / 32;
+  int r;
+  int64_t srcoff;
+  if (q < 512) {  // code chunk: box j, row r, stored chunk pc -> logical chunk pc ^ (r & 7)
+    const int j = q >> 7, within = q & 127;
+    r = within >> 3;
+    const int lc = (within & 7) ^ (r & 7);
+    srcoff = K / 32 + (int64_t)c * DR_CK + j * 128 + lc * 16;
+  } else {  // scales of row r
+    r = q - 512;
+    srcoff = (int64_t)c * 16;
+  }
+  const int64_t row = f2 ? (r < 8 ? t * 8 + r : (int64_t)f2 + t * 8 + (r - 8)) : t * 16 + r;
+  *reinterpret_cast<uint4*>(dst + e * 16) = *reinterpret_cast<const uint4*>(W + row * rb + srcoff);
+}
+
+int dr_repack(const uint8_t* W, int64_t rows, int K, int f2, uint8_t* dst, cudaStream_t st) {
+  Q8_CHECK_ARG(K % DR_CK == 0 && rows % 16 == 0 && (f2 == 0 || 2 * (int64_t)f2 == rows),
+               "ring layout: unsupported matrix %lld x %d", (long long)rows, K);
+  const int C = K / DR_CK;
+  const int64_t n = rows / 16 * C * (DR_BLOCK / 16);
+  k_ring_pack<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(W, n, K, C, f2, dst);
+  return launch_check("k_ring_pack");
 }
 
 // ------------------------------------------------------------------ host side
 size_t dr_apart_floats(int nkv, int nsplit, int hd) {
   return (size_t)nkv * nsplit * (DR_GMAX * hd + 2 * DR_GMAX + 4);
+}
+
+// Partial slots per down-projection tile: a tile of C stages meets at most
+// ceil((C - 1) / per) + 1 of the split ranges (each >= per stages).
+int dr_down_nsf(int H, int F, int G) {
+  const int C = F / DR_CK;
+  const long long S = (long long)(H / 16) * C;
+  const long long per = S / dr_split_ctas(S, C, G);
+  return (int)((C - 2 + per) / per + 1);
 }
 
 int dr_nsplit(int G, int nkv) { return std::max(1, std::min(DR_MAXSPLIT, G / std::max(1, nkv))); }
@@ -1005,14 +1097,8 @@ bool dr_supported(int H, int nh, int nkv, int hd, int F, int V, int page, const 
   if (!fits(H, nqkv / 16, false) || !fits(qd, H / 16, false) || !fits(H, F / 8, false) || !fits(F, H / 16, true) ||
       !fits(H, V / 16, false))
     return no("staging area too small");
-  // the down projection is split evenly over min(G, S) CTAs: a tile of C
-  // stages meets at most ceil((C - 1) / per) + 1 <= DR_NS of them
-  {
-    const int C = F / DR_CK;
-    const long long S = (long long)(H / 16) * C;
-    const long long per = S / std::min((long long)G, S);
-    if ((C - 2 + per) / per + 1 > DR_NS) return no("down tiles would span too many CTAs");
-  }
+  if (H > 16 * DR_CW * 32) return no("hidden wider than the one-item-per-thread RMSNorm staging");
+  if (dr_down_nsf(H, F, G) > DR_NS) return no("down tiles would span too many CTAs");
   return true;
 }
 

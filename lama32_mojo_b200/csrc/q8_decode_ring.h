@@ -3,23 +3,31 @@
 #pragma once
 #include "q8_common.cuh"
 
+#include <cuda.h>
+
 namespace q8 {
 
 constexpr int DR_CW = 8;                         // consumer warps
 constexpr int DR_THREADS = (DR_CW + 1) * 32;     // + one producer warp
 constexpr int DR_SLOTS = 2 * DR_CW;              // ring slots, two per consumer warp
 constexpr int DR_CK = 512;                       // code bytes of one row in a GEMV stage
-constexpr int DR_RS = DR_CK + 16;                // padded row stride in shared memory
-constexpr int DR_SLOT_BYTES = 16 * DR_RS + 16 * 16;  // 16 code rows + their 16 x 8 group scales
+// A ring block: 16 rows x 512 codes as four 16 x 128 B boxes (16-byte chunk c
+// of row r stored at chunk c ^ (r & 7)), then the rows' 16 x 8 f16 group
+// scales.  Weights are copied once into this block order ("ring layout"), so
+// that every stage is one bulk copy.
+constexpr int DR_BLOCK = 16 * DR_CK + 16 * 16;   // 8448 bytes
+constexpr int DR_SLOT_BYTES = DR_BLOCK;
 constexpr int DR_XQ_BYTES = 48 * 1024;           // activation digits + per-warp tile sums
-constexpr int DR_NS = 4;                         // partial slots of a down tile shared by CTAs
+constexpr int DR_NS = 3;                         // partial slots of a down tile shared by CTAs
 constexpr int DR_GMAX = 4;                       // q heads per kv head
 constexpr int DR_MAXSPLIT = 128;                 // attention context splits per kv head
 
 struct DrLayer {
-  const uint8_t* qkv;  // packed [nq*hd + 2*nkv*hd rows][H]
+  // each matrix in ring layout: block (t, c) of 16-row tile t and 512-code
+  // chunk c at (t * K/512 + c) * DR_BLOCK (gate|up tiles: 8 gate + 8 up rows)
+  const uint8_t* qkv;  // [nq*hd + 2*nkv*hd rows][H]
   const uint8_t* o;    // [H rows][nq*hd]
-  const uint8_t* gu;   // [2F rows][H]: F gate rows then F up rows
+  const uint8_t* gu;   // [2F rows][H]: tile t = gate rows t*8.. and up rows t*8..
   const uint8_t* down; // [H rows][F]
   const uint16_t* in_norm;
   const uint16_t* post_norm;
@@ -34,7 +42,7 @@ struct DrParams {
   float eps;
   const DrLayer* layers;       // device array [L]
   const uint8_t* embed;        // packed [vocab][H]
-  const uint8_t* lm_head;      // packed [V][H]
+  const uint8_t* lm_head;      // [V][H] in ring layout
   const uint16_t* final_norm;
   int32_t* ids;                // [1] token of the step (the generate epilogue writes the next one)
   int32_t* pos;                // [1] its position
@@ -47,7 +55,8 @@ struct DrParams {
   // L2-coherent loads
   float* h0;                   // residual of even layers [H]
   float* h1;                   // residual of odd layers [H]
-  float* pres;                 // down-projection partial slots [DR_NS][H]
+  float* pres;                 // down-projection partial slots [nsf][H]
+  int nsf;                     // slots per down tile (every one written each step)
   float* qkv;                  // [nqkv]
   float* ao;                   // attention output [qd]
   float* act;                  // SwiGLU output [F]
@@ -64,6 +73,8 @@ struct DrParams {
   int hist_cap;
   unsigned int* bar;           // grid barrier arrivals (zeroed before each launch)
   int* status;                 // device status word (zero at rest)
+  unsigned long long* trace;   // optional: CTA 0's globaltimer marks [phase][4] (wait done, staged,
+                               // streamed, arrived)
 };
 
 // Host side (q8_decode_ring.cu).
@@ -73,6 +84,10 @@ bool dr_supported(int H, int nh, int nkv, int hd, int F, int V, int page, const 
 int dr_prepare(int hd, int* grid);  // kernel attributes, residency check; grid = CTAs (one per SM)
 size_t dr_apart_floats(int nkv, int nsplit, int hd);
 int dr_nsplit(int G, int nkv);
+int dr_down_nsf(int H, int F, int G);
 int dr_launch(const DrParams& p, int grid, cudaStream_t st);
+// Copies a packed-row matrix (rows x K, SwiGLU: 2 F rows with f2 = F) into
+// ring layout at dst (rows * (K + K/32) bytes).
+int dr_repack(const uint8_t* W, int64_t rows, int K, int f2, uint8_t* dst, cudaStream_t st);
 
 }  // namespace q8

@@ -481,6 +481,33 @@ static PFN_encodeTiled_t encode_fn() {
   return fn;
 }
 
+// 2-D tensor map over `rows` rows of `inner` elements (dtype 0: u8, 1: u16,
+// 2: f32), `row_bytes` apart; box box_inner x box_rows, optionally with the
+// 128 B swizzle.
+int tensor_map_2d(CUtensorMap* m, int dtype, const void* base, uint64_t inner, uint64_t rows, uint64_t row_bytes,
+                  uint32_t box_inner, uint32_t box_rows, bool swizzle128) {
+  PFN_encodeTiled_t enc = encode_fn();
+  if (!enc) {
+    set_error("tensor map: cuTensorMapEncodeTiled unavailable");
+    return Q8_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  const CUtensorMapDataType dt = dtype == 0 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                 : dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT16
+                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("tensor map: encode failed (%d)", (int)r);
+    return Q8_ERR_CUDA;
+  }
+  return Q8_OK;
+}
+
 // 2-D tensor map over `rows` rows of `inner` f32 elements, `row_bytes` apart
 // (the decode attention's K pool); box box_inner x box_rows, 128 B swizzle.
 int tensor_map_f32_rows(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t row_bytes,

@@ -2,6 +2,8 @@
 #pragma once
 #include "q8_common.cuh"
 
+#include <cuda.h>
+
 namespace q8 {
 
 enum { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
@@ -43,6 +45,10 @@ int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int64_t x16lo, int 
                    float* y, int64_t ldy, __half* y16, int64_t ldy16, int64_t y16lo, cudaStream_t st);
 // After a synchronize: Q8_OK, or the timeout a pipeline wait recorded (cleared).
 int gemm_tc_poll_error();
+// 2-D tensor map (cuTensorMapEncodeTiled) over `rows` rows of `inner`
+// elements (dtype 0: u8, 1: u16, 2: f32) `row_bytes` apart.
+int tensor_map_2d(CUtensorMap* m, int dtype, const void* base, uint64_t inner, uint64_t rows, uint64_t row_bytes,
+                  uint32_t box_inner, uint32_t box_rows, bool swizzle128);
 // Device address of the error word of the tensor-core GEMM file (read
 // asynchronously by the model calls together with their results).
 int gemm_tc_error_word(int** out);

@@ -215,7 +215,12 @@ struct q8_ctx {
   int *dr_aticket = nullptr, *dr_lm_ticket = nullptr, *dr_status = nullptr, *dr_status_pin = nullptr;
   unsigned long long* dr_amax = nullptr;
   unsigned int* dr_bar = nullptr;
+  uint8_t* dr_wring = nullptr;  // the weight arena again, matrices in ring layout (q8_decode_ring.cu)
+  bool dr_packed = false;       // dr_wring matches the loaded weights
+  unsigned long long* dr_trace = nullptr;  // CTA 0's phase marks of the last profiled ring step
+  bool dr_traced = false;
   double dr_wbytes = 0;  // weight bytes one step streams
+  double dr_kv_bytes = 0;
   float *xn32 = nullptr, *ao32 = nullptr, *act32 = nullptr;  // f32 copies of the GEMV inputs
   float *am_val = nullptr, *am_gval = nullptr, *lg_gather = nullptr;
   int32_t *am_idx = nullptr, *am_gidx = nullptr;
@@ -291,6 +296,25 @@ static int allreduce(q8_ctx* c, float* buf, size_t n) {
 // batch is too large for it, so the caller keeps NCCL + the RMSNorm kernel.
 static bool p2p_fits(q8_ctx* c, int T) { return c->ar.ok && (int64_t)T * c->H <= c->ar.slot; }
 
+// Ring-layout copy of every matrix the ring step streams, made once after
+// the weights are loaded (and again after a reload), outside graph capture.
+static int ring_prepare(q8_ctx* c) {
+  if (!c->dr || c->dr_packed) return Q8_OK;
+  const int H = c->H, nqkv = c->qd + 2 * c->kvd;
+  auto rp = [&](const uint8_t* w) { return c->dr_wring + (w - c->warena); };
+  for (int L = 0; L < c->cfg.layers; ++L) {
+    const LayerW& w = c->layers[L];
+    Q8_TRY(dr_repack(w.qkv, nqkv, H, 0, rp(w.qkv), c->st));
+    Q8_TRY(dr_repack(w.o, H, c->qd, 0, rp(w.o), c->st));
+    Q8_TRY(dr_repack(w.gu, 2 * (int64_t)c->F, H, c->F, rp(w.gu), c->st));
+    Q8_TRY(dr_repack(w.down, H, c->F, 0, rp(w.down), c->st));
+  }
+  Q8_TRY(dr_repack(c->lm_head, c->V_loc, H, 0, rp(c->lm_head), c->st));
+  Q8_CUDA(cudaStreamSynchronize(c->st));
+  c->dr_packed = true;
+  return Q8_OK;
+}
+
 // Whether a step of T tokens runs as one weight-ring launch (one decode
 // token, greedy, the whole vocabulary on this GPU).
 static bool ring_ok(q8_ctx* c, int T, bool blocks, int lrow0, int lrows) {
@@ -303,14 +327,17 @@ static int ring_step(q8_ctx* c, bool gen) {
   DrParams p{};
   p.H = c->H; p.nh = c->nh; p.nkv = c->nkv; p.hd = c->hd; p.qd = c->qd; p.nqkv = c->qd + 2 * c->kvd;
   p.F = c->F; p.V = c->V; p.L = c->cfg.layers; p.eps = c->cfg.eps;
-  p.layers = c->dr_layers; p.embed = c->embed; p.lm_head = c->lm_head; p.final_norm = c->final_norm;
+  p.layers = c->dr_layers; p.embed = c->embed; p.lm_head = c->dr_wring + (c->lm_head - c->warena);
+  p.final_norm = c->final_norm;
   p.ids = c->ids_d; p.pos = c->pos_d; p.seq = c->seq_d; p.inv_freq = c->inv_freq_d;
   p.page = c->page; p.bt = c->bt_d; p.max_pages = c->max_pages;
-  p.h0 = c->h; p.h1 = c->dr_h1; p.pres = c->dr_pres; p.qkv = c->qkv; p.ao = c->ao32; p.act = c->act32;
+  p.h0 = c->h; p.h1 = c->dr_h1; p.pres = c->dr_pres; p.nsf = dr_down_nsf(c->H, c->F, c->dr_grid); p.qkv = c->qkv; p.ao = c->ao32; p.act = c->act32;
   p.logits = c->logits; p.apart = c->dr_apart; p.aticket = c->dr_aticket; p.nsplit = c->dr_nsplit;
   p.amax = c->dr_amax; p.lm_ticket = c->dr_lm_ticket; p.argmax = c->argmax_d;
   p.gen = gen ? 1 : 0; p.hist = c->hist_d; p.ctr = c->ctr_d; p.hist_cap = c->hist_cap;
   p.bar = c->dr_bar; p.status = c->dr_status;
+  p.trace = c->profiling ? c->dr_trace : nullptr;
+  c->dr_traced = c->profiling;
   return dr_launch(p, c->dr_grid, c->st);
 }
 
@@ -680,7 +707,7 @@ static int destroy_impl(q8_ctx* c) {
                   c->qb_tok0_d, c->qb_len_d, c->argmax_d, c->hist_d, c->ctr_d, c->ticket_d, c->h, c->qkv, c->ypart,
                   c->logits, c->part, c->xs_in, c->xs_ao, c->xs_act, c->xn32, c->ao32, c->act32, c->am_val, c->am_gval, c->lg_gather,
                   c->am_idx, c->am_gidx, c->dr_layers, c->dr_h1, c->dr_pres, c->dr_apart, c->dr_aticket,
-                  c->dr_lm_ticket, c->dr_status, c->dr_amax, c->dr_bar,
+                  c->dr_lm_ticket, c->dr_status, c->dr_amax, c->dr_bar, c->dr_trace, c->dr_wring,
                   c->samp_ws, c->samp_u, c->samp_logits};
   for (void* p : ptrs)
     if (p) cudaFree(p);
@@ -938,14 +965,17 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
       if (cudaMallocHost((void**)&c->dr_status_pin, 4) != cudaSuccess)
         return bail((set_error("cudaMallocHost failed"), Q8_ERR_OOM));
       *c->dr_status_pin = 0;
+      if ((s = dmalloc((void**)&c->dr_wring, c->wbytes))) return bail(s);
+      auto rp = [&](const uint8_t* w) { return (const uint8_t*)(c->dr_wring + (w - c->warena)); };
       std::vector<DrLayer> dl(C.layers);
       for (int L = 0; L < C.layers; ++L) {
         const LayerW& w = c->layers[L];
-        dl[L] = DrLayer{w.qkv, w.o, w.gu, w.down, w.in_norm, w.post_norm, w.q_norm, w.k_norm,
+        dl[L] = DrLayer{rp(w.qkv), rp(w.o), rp(w.gu), rp(w.down), w.in_norm, w.post_norm, w.q_norm, w.k_norm,
                         c->kpool + (size_t)L * c->layer_kv, c->vpool + (size_t)L * c->layer_kv};
       }
       if (cudaMemcpy(c->dr_layers, dl.data(), sizeof(DrLayer) * C.layers, cudaMemcpyHostToDevice) != cudaSuccess)
         return bail((set_error("decode step layer table upload failed"), Q8_ERR_CUDA));
+      if ((s = dmalloc((void**)&c->dr_trace, sizeof(unsigned long long) * 4 * (5 * C.layers + 1)))) return bail(s);
       c->dr_wbytes = (double)C.layers * ((double)nqkv * q8_row_bytes(H) + (double)H * q8_row_bytes(c->qd) +
                                          2.0 * c->F * q8_row_bytes(H) + (double)H * q8_row_bytes(c->F)) +
                      (double)c->V * q8_row_bytes(H);
@@ -1066,6 +1096,7 @@ static int load_tensor_impl(q8_ctx* c, const char* cname, int dtype, int64_t row
   ShardPlan p;
   Q8_TRY(shard_plan(c->cfg, c->tp_rank, c->tp_size, name, p));
   if (p.slot.empty()) return Q8_OK;  // not used by the Q8 path (or a tied lm_head)
+  c->dr_packed = false;  // the ring-layout copy is remade before the next ring step
   const int64_t gotm = (cols == 0) ? 1 : cols;
   if (rows != p.n || gotm != p.m) {
     set_error("tensor %s: expected logical shape [%lld, %lld], got [%lld, %lld]", cname, (long long)p.n,
@@ -1252,6 +1283,7 @@ static int forward_impl(q8_ctx* c, const int32_t* ids, int s, int seq, float* lo
   Q8_CHECK_ARG(seq >= 0 && seq < c->max_seqs, "q8_forward: seq %d out of range", seq);
   Q8_CUDA(cudaSetDevice(c->dev));
   Q8_TRY(check_ready(c));
+  Q8_TRY(ring_prepare(c));
   if (c->n_cached[seq] + s > c->maxlen) {
     set_error("KV cache full: seq %d has %d cached, +%d > maxlen %d", seq, c->n_cached[seq], s, c->maxlen);
     return Q8_ERR_KV_FULL;
@@ -1317,6 +1349,7 @@ static int forward_hidden_impl(q8_ctx* c, const int32_t* ids, int s, int seq, in
   Q8_CHECK_ARG(seq >= 0 && seq < c->max_seqs && layer >= 0 && layer < c->cfg.layers, "q8_forward_hidden: bad seq/layer");
   Q8_CUDA(cudaSetDevice(c->dev));
   Q8_TRY(check_ready(c));
+  Q8_TRY(ring_prepare(c));
   if (c->n_cached[seq] + s > c->maxlen) {
     set_error("KV cache full");
     return Q8_ERR_KV_FULL;
@@ -1433,6 +1466,7 @@ static int decode_impl(q8_ctx* c, const int32_t* ids, const int32_t* seqs, int B
   Q8_CHECK_ARG(c && ids && seqs, "q8_decode: null argument");
   Q8_CUDA(cudaSetDevice(c->dev));
   Q8_TRY(check_ready(c));
+  Q8_TRY(ring_prepare(c));
   std::vector<int> lens;
   Q8_TRY(stage_decode(c, ids, seqs, B, lens));
   c->prof.clear();
@@ -1462,6 +1496,7 @@ static int generate_impl(q8_ctx* c, const int32_t* first, const int32_t* seqs, i
   Q8_CHECK_ARG(steps <= c->hist_cap, "q8_generate: steps %d > %d per call", steps, c->hist_cap);
   Q8_CUDA(cudaSetDevice(c->dev));
   Q8_TRY(check_ready(c));
+  Q8_TRY(ring_prepare(c));
   if (steps == 0) return Q8_OK;
   for (int b = 0; b < B; ++b) {
     Q8_CHECK_ARG(seqs[b] >= 0 && seqs[b] < c->max_seqs, "q8_generate: bad seq");
@@ -1577,6 +1612,35 @@ int q8_profile(const q8_ctx* ctx, int cap, const char** names, double* ms, doubl
     tms[e.name] += t;
     tb[e.name] += e.bytes;
     cnt[e.name] += 1;
+  }
+  // phases of the last profiled ring step as CTA 0 saw them, summed over the
+  // layers: wait (for the previous phase of the whole grid), stage (the
+  // activation vector; the whole attention for attention phases), stream
+  // (the CTA's ring stages), epi (epilogue stores and arrival)
+  if (ctx->dr_traced && ctx->dr_trace) {
+    const int L = ctx->cfg.layers, nph = 5 * L + 1;
+    std::vector<unsigned long long> t((size_t)4 * nph);
+    if (cudaMemcpy(t.data(), ctx->dr_trace, t.size() * 8, cudaMemcpyDeviceToHost) == cudaSuccess) {
+      const char* kn[6] = {"qkv", "attn", "o", "gateup", "down", "lmhead"};
+      const char* pn[4] = {"wait", "stage", "stream", "epi"};
+      double acc[6][4] = {};
+      for (int ph = 0; ph < nph; ++ph) {
+        const int k = ph == 5 * L ? 5 : ph % 5;
+        const unsigned long long* m = t.data() + 4 * ph;
+        if (ph > 0) acc[k][0] += (double)(m[0] - t[4 * (ph - 1) + 3]) * 1e-6;
+        for (int j = 1; j < 4; ++j) acc[k][j] += (double)(m[j] - m[j - 1]) * 1e-6;
+      }
+      for (int k = 0; k < 6; ++k)
+        for (int j = 0; j < 4; ++j) {
+          const std::string nm = std::string("phase:") + kn[k] + "." + pn[j];
+          order.push_back(nm);
+          tms[nm] = acc[k][j];
+          tb[nm] = 0;
+          cnt[nm] = 0;
+        }
+    } else {
+      cudaGetLastError();
+    }
   }
   int k = 0;
   static thread_local std::vector<std::string> keep;

@@ -76,26 +76,29 @@ def sample(logits: np.ndarray, temp: float, top_p: float, u: float):
 
 
 def _rand_packed(rng, n, m):
-    """Random packed rows: f16 scales ~ 0.02*2.5/127 and uniform int8 codes."""
+    """Random packed rows: f16 scales ~ 0.02*2.5/127 and uniform int8 codes in
+    [-127, 127] (random bytes, -128 moved to -127 as the quantizer never
+    writes it)."""
     sc = (np.full((n, m // 64), 0.02 * 2.5 / 127, np.float32)).astype(np.float16).view(np.uint16)
-    q = rng.integers(-127, 128, size=(n, m), dtype=np.int8).view(np.uint8)
     out = np.empty((n, m // 32 + m), np.uint8)
     out[:, : m // 32] = sc.view(np.uint8).reshape(n, m // 32)
-    out[:, m // 32:] = q
+    q = np.frombuffer(rng.bytes(n * m), np.int8).reshape(n, m)
+    out[:, m // 32:] = np.maximum(q, np.int8(-127)).view(np.uint8)
     return out
 
 
-def time_decode_sample(cfg, batch: int, ctx: int, sample_layers: int = 2, steps: int = 2, seed: int = 0):
-    """Time the CPU port of one decode step on a bounded sample: ``sample_layers``
-    full-width layers (the reference's run_layer_q8 for one token) plus the
-    final norm + lm_head GEMV + argmax, with a ``ctx``-long f32 KV cache.  The
-    full-model step time is layers_time * (cfg.layers / sample_layers) +
-    head_time; batch B is B single-sequence decodes (the reference decodes one
-    sequence).  Returns tok/s and the sample description."""
+def time_decode_sample(cfg, batch: int, ctx: int, sample_layers: int = 0, steps: int = 2, seed: int = 0):
+    """Time the CPU port of decode steps: ``sample_layers`` full-width layers
+    (0: every layer of the model; the reference's run_layer_q8 for one token)
+    plus the final norm + lm_head GEMV + argmax, with a ``ctx``-long f32 KV
+    cache.  With fewer layers than the model the step time is layers_time *
+    (cfg.layers / sample_layers) + head_time; batch B is B single-sequence
+    decodes (the reference decodes one sequence).  Returns tok/s and the
+    sample description."""
     L = lib()
     rng = np.random.default_rng(seed)
     H, QD, KVD, F, hd = cfg.hidden, cfg.q_dim, cfg.kv_dim, cfg.inter, cfg.head_dim
-    ls = max(1, min(sample_layers, cfg.layers))
+    ls = cfg.layers if sample_layers <= 0 else max(1, min(sample_layers, cfg.layers))
     ones = np.full(H, 0x3F80, np.uint16)
     hones = np.full(hd, 0x3F80, np.uint16)
     keep = []
@@ -136,8 +139,11 @@ def time_decode_sample(cfg, batch: int, ctx: int, sample_layers: int = 2, steps:
     per_tok = (t_layers / nrun) * (cfg.layers / ls) + t_head / nrun
     return {"tok_s": 1.0 / per_tok, "ms_per_step": per_tok * batch * 1e3, "threads": L.q8r_threads(),
             "steps": steps,
-            "sample": f"{ls} of {cfg.layers} full-width layers + lm_head per token at ctx {ctx}, "
-                      f"{steps} timed steps x batch {batch}; layer time scaled by {cfg.layers}/{ls}"}
+            "sample": (f"full {cfg.layers}-layer decode step + lm_head per token at ctx {ctx}, "
+                       f"{steps} timed steps x batch {batch} (random packed weights, one warm-up step)"
+                       if ls == cfg.layers else
+                       f"{ls} of {cfg.layers} full-width layers + lm_head per token at ctx {ctx}, "
+                       f"{steps} timed steps x batch {batch}; layer time scaled by {cfg.layers}/{ls}")}
 
 
 class RefModel:
