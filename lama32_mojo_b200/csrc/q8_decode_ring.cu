@@ -312,31 +312,37 @@ __device__ __forceinline__ void dr_digits16(const float (&v)[16], bool valid, in
   if (!valid) return;
   const float e = amax / 127.0f;
   const float ie = amax > 0.f ? 127.0f / amax : 0.f;
-  uint32_t w[3][4];
+  uint8_t* dq = xq + (int64_t)gi * 192 + sq * 4;
+  // Round-to-nearest-even through the f32 adder: for |x| < 2^22, y = x +
+  // 1.5 * 2^23 holds rint(x) exactly, y - 1.5 * 2^23 is that integer as a
+  // float and the low byte of y's bits is it modulo 256 (the conversion
+  // instructions run at a fraction of the adder's rate).  Every digit is
+  // within [-127, 127]: |x| <= 127 for the first, |residual| <= 0.5 * 254 for
+  // the others.
+  constexpr float kM = 12582912.0f;
 #pragma unroll
   for (int t = 0; t < 4; ++t) {
-    uint32_t p0 = 0, p1 = 0, p2 = 0;
+    uint32_t y0[4], y1[4], y2[4];
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
-      float x = v[4 * t + b] * ie;
-      const int d0 = max(-127, min(127, __float2int_rn(x)));
-      x = (x - (float)d0) * 254.0f;
-      const int d1 = max(-127, min(127, __float2int_rn(x)));
-      x = (x - (float)d1) * 254.0f;
-      const int d2 = max(-127, min(127, __float2int_rn(x)));
-      p0 |= (uint32_t)(d0 & 0xFF) << (8 * b);
-      p1 |= (uint32_t)(d1 & 0xFF) << (8 * b);
-      p2 |= (uint32_t)(d2 & 0xFF) << (8 * b);
+      const float x = v[4 * t + b] * ie;
+      const float r0 = __fadd_rn(x, kM);
+      const float x1 = __fmul_rn(__fsub_rn(x, __fsub_rn(r0, kM)), 254.0f);
+      const float r1 = __fadd_rn(x1, kM);
+      const float x2 = __fmul_rn(__fsub_rn(x1, __fsub_rn(r1, kM)), 254.0f);
+      const float r2 = __fadd_rn(x2, kM);
+      y0[b] = __float_as_uint(r0);
+      y1[b] = __float_as_uint(r1);
+      y2[b] = __float_as_uint(r2);
     }
-    w[0][t] = p0;
-    w[1][t] = p1;
-    w[2][t] = p2;
+    // low bytes of the four values, in value order
+    *reinterpret_cast<uint32_t*>(dq + t * 16) =
+        __byte_perm(__byte_perm(y0[0], y0[1], 0x0040), __byte_perm(y0[2], y0[3], 0x0040), 0x5410);
+    *reinterpret_cast<uint32_t*>(dq + 64 + t * 16) =
+        __byte_perm(__byte_perm(y1[0], y1[1], 0x0040), __byte_perm(y1[2], y1[3], 0x0040), 0x5410);
+    *reinterpret_cast<uint32_t*>(dq + 128 + t * 16) =
+        __byte_perm(__byte_perm(y2[0], y2[1], 0x0040), __byte_perm(y2[2], y2[3], 0x0040), 0x5410);
   }
-  uint8_t* dq = xq + (int64_t)gi * 192 + sq * 4;
-#pragma unroll
-  for (int dg = 0; dg < 3; ++dg)
-#pragma unroll
-    for (int t = 0; t < 4; ++t) *reinterpret_cast<uint32_t*>(dq + dg * 64 + t * 16) = w[dg][t];
   if (sq == 0) fcol[gi] = make_float4(e, e / 254.0f, e / 64516.0f, 0.f);
 }
 

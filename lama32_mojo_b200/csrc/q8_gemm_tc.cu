@@ -682,7 +682,9 @@ int gemm_tc_launch(int epi, const __half* x16, int64_t ld16, int64_t x16lo, int 
 int tc_min_tokens() {
   static const int v = [] {
     const char* e = getenv("Q8_TC_MIN");
-    return e ? std::max(1, atoi(e)) : kTcMinTokens;
+    // the tensor-core GEMM (64-token tiles, split K) beats the split-f16
+    // GEMV from 16 tokens, as in the model's decode batches
+    return e ? std::max(1, atoi(e)) : kTcDecodeMinTokens;
   }();
   return v;
 }

@@ -56,7 +56,9 @@ int gemm_tc_error_word(int** out);
 int gemm_tc_prepare();
 // Smallest token batch the model runtime sends to the tensor-core GEMM.
 constexpr int kTcMinTokens = 128;
-// token count from which batches use the tensor-core GEMM (Q8_TC_MIN, default kTcMinTokens)
+// Token count from which op-level GEMMs and decode steps take the tensor-core GEMM.
+constexpr int kTcDecodeMinTokens = 16;
+// token count from which op-level GEMMs use the tensor-core GEMM (Q8_TC_MIN, default kTcDecodeMinTokens)
 int tc_min_tokens();
 // x (Q8_F32 / Q8_BF16 / Q8_F16 rows) -> plain f16 rows [M][K].
 int to_f16_launch(const void* x, int dtype, int64_t ldx, int M, int K, __half* y, cudaStream_t st,

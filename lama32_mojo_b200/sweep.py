@@ -6,8 +6,9 @@
 Every projection shape of Llama-3.2-1B / 3B (K x N), int8 weights from N(0, 0.02)
 with group-64 f16 scales packed by the GPU packer, bf16 activations N(0, 1),
 M tokens.  Each case times ``q8op_gemm`` with CUDA events on the current stream
-after warm-up, rotating over enough weight copies that every launch reads
-weights from HBM (> 126 MB L2 per rotation), and prints one JSON line with the
+after warm-up (the timed launches captured in one CUDA graph), rotating over
+enough weight copies that every launch reads weights from HBM (> 126 MB L2
+per rotation), and prints one JSON line with the
 achieved HBM GB/s (algorithmic bytes: codes + scales + activations + output)
 and TFLOP/s (2*M*N*K).  ``--one`` runs a single case (the small command used
 for ncu captures).
@@ -54,10 +55,17 @@ def run_case(K, N, M, iters=20, warmup=5):
     for i in range(warmup):
         ops.mm_q8(x, ws[i % copies], K, out=y)
     torch.cuda.synchronize()
+    # the timed launches replay a CUDA graph, so that the host's launch rate
+    # (a ctypes call per GEMM) does not leave the GPU idle between kernels
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(iters):
+            ops.mm_q8(x, ws[i % copies], K, out=y)
+    g.replay()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for i in range(iters):
-        ops.mm_q8(x, ws[i % copies], K, out=y)
+    g.replay()
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / iters
