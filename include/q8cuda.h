@@ -72,6 +72,10 @@ typedef struct q8_config {
   int32_t rope_type;
   int32_t qk_norm;
   int32_t tied;
+  /* Q8_BF16: keep the linear weights as bf16 (the reference's non-Q8 path,
+   * run_layer, src/llama_common.mojo:697-780); anything else (0 or
+   * Q8_PACKED): Q8 group-64 weights. */
+  int32_t weight_dtype;
 } q8_config;
 
 typedef struct q8_ctx q8_ctx;
@@ -129,6 +133,13 @@ int q8op_gemm(const void* x, int x_dtype, int64_t ldx, int64_t M, int64_t K,
 #define Q8_NOALLOC_MAX_ELEMS (2 * 1024 * 1024)
 int q8op_gemm_noalloc(const void* x, int x_dtype, int64_t ldx, int64_t M, int64_t K,
                       const void* packed_w, int64_t N, float* y, int64_t ldy, void* stream);
+
+/* bf16-weight product y[M, N] = x[M, K] . W[N, K]^T, x f32 rows, W plain bf16
+ * rows (no quantization), f32 accumulation — the reference's non-Q8 matmul
+ * k_mm_w / k_mm_tile behind mm_op (src/llama_common.mojo:89-162, :636-684).
+ * K % 8 == 0; x, W 16-byte aligned, ldx % 4 == 0. */
+int q8op_gemm_bf16(const float* x, int64_t ldx, int64_t M, int64_t K, const void* w_bf16, int64_t N,
+                   float* y, int64_t ldy, void* stream);
 
 /* Fused gate|up GEMV + SwiGLU: act[M, F] = silu(x.Wg^T) * (x.Wu^T) where
  * packed_gu holds the F gate rows followed by the F up rows — replaces the

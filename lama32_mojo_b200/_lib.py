@@ -24,7 +24,7 @@ class q8_config(C.Structure):
                 ("vocab", C.c_int32), ("eps", C.c_float), ("theta", C.c_double),
                 ("rope_factor", C.c_double), ("low_ff", C.c_double), ("high_ff", C.c_double),
                 ("orig_ctx", C.c_double), ("rope_type", C.c_int32), ("qk_norm", C.c_int32),
-                ("tied", C.c_int32)]
+                ("tied", C.c_int32), ("weight_dtype", C.c_int32)]
 
 
 class Q8Error(RuntimeError):
@@ -56,6 +56,7 @@ SIGNATURES = {
     "q8op_gemm": [_P, _I32, _I64, _I64, _I64, _P, _I64, _P, _I64, _P],
     "q8op_gemm_noalloc": [_P, _I32, _I64, _I64, _I64, _P, _I64, _P, _I64, _P],
     "q8op_gemm_swiglu": [_P, _I32, _I64, _I64, _I64, _P, _I64, _P, _I64, _P],
+    "q8op_gemm_bf16": [_P, _I64, _I64, _I64, _P, _I64, _P, _I64, _P],
     "q8op_embed": [_P, _I64, _I64, _P, _I64, _P, _P],
     "q8op_rmsnorm": [_P, _P, _P, _I64, _I64, _F, _P, _P],
     "q8op_rmsnorm_heads": [_P, _P, _I64, _I64, _F, _P, _P],

@@ -35,6 +35,9 @@ class Config:
     orig_ctx: float = 8192.0
     qk_norm: bool = False
     tied: bool = True
+    # "q8": packed Q8 matrices (the default); "bf16": the reference's non-Q8
+    # path (run_layer / mm_op, src/llama_common.mojo:636-780), weights kept bf16
+    weights: str = "q8"
 
     @property
     def q_dim(self) -> int:
@@ -52,7 +55,8 @@ class Config:
             self.hidden, self.layers, self.n_heads, self.n_kv, self.head_dim, self.inter, self.vocab,
             self.eps, self.theta, self.rope_factor, self.low_ff, self.high_ff, self.orig_ctx,
             _lib.Q8_ROPE_LLAMA3 if self.rope_type == "llama3" else _lib.Q8_ROPE_DEFAULT,
-            int(self.qk_norm), int(self.tied))
+            int(self.qk_norm), int(self.tied),
+            _lib.Q8_BF16 if self.weights == "bf16" else _lib.Q8_PACKED)
 
     def weight_names(self) -> List[str]:
         """Tensor names the model loads (src/llama_gpu.mojo:34-49, qwen_q8.mojo:35-52)."""
@@ -90,11 +94,13 @@ class Config:
         return per_layer * self.layers + self.vocab * H
 
     def decode_bytes(self, batch: int, ctx: int, tp: int = 1, kv_bytes: int = 4) -> float:
-        """Algorithmic HBM bytes of one decode step per GPU: every Q8 weight byte
-        once (int8 codes + f16 group scales) plus the KV read of ``ctx`` positions."""
+        """Algorithmic HBM bytes of one decode step per GPU: every weight byte
+        once (Q8: int8 codes + f16 group scales; bf16: 2 bytes) plus the KV read
+        of ``ctx`` positions."""
         H, QD, KVD, F = self.hidden, self.q_dim, self.kv_dim, self.inter
         per_layer = (QD + 2 * KVD) * H + H * QD + 2 * F * H + H * F
-        w = (per_layer * self.layers + self.vocab * H) * (1 + 2 / 64) / tp
+        wb = 2.0 if self.weights == "bf16" else 1 + 2 / 64
+        w = (per_layer * self.layers + self.vocab * H) * wb / tp
         kv = batch * ctx * self.layers * 2 * (KVD / tp) * kv_bytes
         return w + kv
 

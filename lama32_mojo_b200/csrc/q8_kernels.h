@@ -64,6 +64,12 @@ int tc_min_tokens();
 int to_f16_launch(const void* x, int dtype, int64_t ldx, int M, int K, __half* y, cudaStream_t st,
                   int64_t ylo = 0);
 
+// bf16-weight products (q8_bf16.cu): y = x . W^T with f32 x rows, epilogue
+// STORE / ADD / SWIGLU (W = gate rows then up rows); bf16 embedding gather.
+int gemm_bf16_launch(int epi, const float* x, int64_t ldx, int M, int K, const uint16_t* W, int N, float* y,
+                     int64_t ldy, cudaStream_t st);
+int embed_bf16_launch(const uint16_t* E, int64_t d, const int32_t* ids, int64_t s, float* y, cudaStream_t st);
+
 int embed_launch(const void* packed_emb, int64_t d, const int32_t* ids, int64_t s, float* y,
                  cudaStream_t st);
 // y32 / yxs / y16 (plain f16 rows, the tensor-core GEMM input) may be null;

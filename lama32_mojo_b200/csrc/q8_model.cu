@@ -207,6 +207,7 @@ struct q8_ctx {
   size_t part_floats = 0;
   __half *xs_in = nullptr, *xs_ao = nullptr, *xs_act = nullptr;
   bool tc = false;  // tensor-core GEMM for prefill batches (every K a multiple of 512)
+  bool bf16 = false;  // linear weights kept as bf16 rows (q8_config.weight_dtype == Q8_BF16)
   // weight-ring decode step (one GPU, one sequence): q8_decode_ring.cu
   bool dr = false;
   int dr_grid = 0, dr_nsplit = 1;
@@ -241,6 +242,9 @@ struct q8_ctx {
   size_t ev_used = 0;
   int prof_depth_guard = 0;
 };
+
+// Bytes of one stored weight row of K inputs: packed Q8, or plain bf16.
+static int64_t wrow_bytes(const q8_ctx* c, int64_t K) { return c->bf16 ? 2 * K : q8_row_bytes(K); }
 
 static int fail_ctx(q8_ctx* c, int s) {
   if (s != Q8_OK && c) c->err = get_error();
@@ -341,6 +345,135 @@ static int ring_step(q8_ctx* c, bool gen) {
   return dr_launch(p, c->dr_grid, c->st);
 }
 
+// Next tokens of logit rows [lrow0, lrow0 + lrows) into argmax_d: sampled
+// (q8_set_sampling) or greedy (k_argmax, src/llama_common.mojo:493-519).
+static int select_tokens(q8_ctx* c, int lrow0, int lrows) {
+  cudaStream_t st = c->st;
+  const bool tp = c->tp_size > 1;
+  if (c->samp_temp > 0.f) {  // sampled tokens into argmax_d
+    cudaEvent_t pe;
+    Q8_TRY(prof_begin(c, &pe));
+    const float* lg = c->logits;
+    if (tp) {  // every rank samples the whole vocabulary with the same draws
+      ncclResult_t r = ncclAllGather(c->logits, c->lg_gather, (size_t)lrows * c->V_loc, ncclFloat, c->comm, st);
+      if (r != ncclSuccess) {
+        set_error("logits allgather: %s", ncclGetErrorString(r));
+        return Q8_ERR_COMM;
+      }
+      for (int k = 0; k < c->tp_size; ++k)  // [tp][rows][V_loc] -> [rows][V]
+        Q8_CUDA(cudaMemcpy2DAsync(c->samp_logits + (size_t)k * c->V_loc, (size_t)c->V * 4,
+                                  c->lg_gather + (size_t)k * lrows * c->V_loc, (size_t)c->V_loc * 4,
+                                  (size_t)c->V_loc * 4, lrows, cudaMemcpyDeviceToDevice, st));
+      lg = c->samp_logits;
+    }
+    k_sample_draws<<<ceil_div(lrows, 128), 128, 0, st>>>(c->pos_d + lrow0, c->seq_d + lrow0, lrows, c->samp_seed,
+                                                         c->samp_u);
+    Q8_TRY(launch_check("k_sample_draws"));
+    Q8_TRY(sample_launch(lg, lrows, c->V, c->V, c->samp_temp, c->samp_top_p, c->samp_u, c->argmax_d, c->samp_ws,
+                         c->samp_ws_bytes, st));
+    Q8_TRY(prof_end(c, "sample", (double)lrows * c->V * 4.0));
+  } else if (!tp) {
+    PROF(c, "argmax", (double)lrows * c->V * 4.0,
+         argmax_launch(c->logits, lrows, c->V, c->V, c->argmax_d, st));
+  } else {
+    cudaEvent_t pe;
+    Q8_TRY(prof_begin(c, &pe));
+    k_argmax_local<<<lrows, 1024, 0, st>>>(c->logits, c->V_loc, c->V_loc, c->am_val, c->am_idx);
+    Q8_TRY(launch_check("k_argmax_local"));
+    ncclGroupStart();
+    ncclAllGather(c->am_val, c->am_gval, lrows, ncclFloat, c->comm, st);
+    ncclAllGather(c->am_idx, c->am_gidx, lrows, ncclInt32, c->comm, st);
+    ncclResult_t r = ncclGroupEnd();
+    if (r != ncclSuccess) {
+      set_error("argmax allgather: %s", ncclGetErrorString(r));
+      return Q8_ERR_COMM;
+    }
+    k_argmax_pick<<<ceil_div(lrows, 128), 128, 0, st>>>(c->am_gval, c->am_gidx, c->tp_size, lrows, c->V_loc,
+                                                         c->argmax_d);
+    Q8_TRY(launch_check("k_argmax_pick"));
+    Q8_TRY(prof_end(c, "argmax", (double)lrows * c->V_loc * 4.0));
+  }
+  return Q8_OK;
+}
+
+// bf16-weight layers: the reference's non-Q8 run_layer
+// (src/llama_common.mojo:697-780) behind mm_op (:636-684).  Standalone
+// RMSNorm into f32 rows, bf16 products with the residual add and SwiGLU fused
+// into their epilogues, the Q8 path's RoPE / KV-append / attention kernels, and
+// a bf16 lm_head (tied: the embedding rows).
+static int run_tokens_bf16(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int nsplit, int lrow0, int lrows,
+                           double kv_bytes_hint) {
+  const int H = c->H;
+  const int nqkv = c->qd + 2 * c->kvd;
+  cudaStream_t st = c->st;
+  const bool tp = c->tp_size > 1;
+  const float eps = c->cfg.eps;
+  auto bw = [](const uint8_t* p) { return reinterpret_cast<const uint16_t*>(p); };
+  auto bytes = [](int64_t M, int64_t K, int64_t N) { return (double)N * K * 2.0 + (double)M * (K + N) * 4.0; };
+  PROF(c, "embed", (double)T * H * 6.0, embed_bf16_launch(bw(c->embed), H, c->ids_d, T, c->h, st));
+  const float* pending = nullptr;  // row-parallel sum not yet added to h (TP prefill)
+  // row-parallel output (o_proj, down): added into h, or summed over ranks
+  auto rowpar = [&](const char* name, const float* x, int K, const uint8_t* W) -> int {
+    if (!tp) {
+      PROF(c, name, bytes(T, K, H), gemm_bf16_launch(EPI_ADD, x, K, T, K, bw(W), H, c->h, H, st));
+      return Q8_OK;
+    }
+    PROF(c, name, bytes(T, K, H), gemm_bf16_launch(EPI_STORE, x, K, T, K, bw(W), H, c->ypart, H, st));
+    if (!blocks && p2p_fits(c, T)) {
+      PROF(c, "allreduce", (double)T * H * 4.0 * c->tp_size, ar_launch(c->ar, c->ypart, c->h, T * H, st));
+    } else {
+      PROF(c, "allreduce", (double)T * H * 4.0, allreduce(c, c->ypart, (size_t)T * H));
+      pending = c->ypart;
+    }
+    return Q8_OK;
+  };
+  for (int L = 0; L < c->cfg.layers; ++L) {
+    const LayerW& w = c->layers[L];
+    PROF(c, "rmsnorm", (double)T * H * (pending ? 16.0 : 8.0),
+         rmsnorm_launch(c->h, pending, w.in_norm, T, H, eps, c->xn32, nullptr, nullptr, st));
+    pending = nullptr;
+    PROF(c, "gemm_qkv", bytes(T, H, nqkv), gemm_bf16_launch(EPI_STORE, c->xn32, H, T, H, bw(w.qkv), nqkv, c->qkv,
+                                                            nqkv, st));
+    float* kp = c->kpool + (size_t)L * c->layer_kv;
+    float* vp = c->vpool + (size_t)L * c->layer_kv;
+    if (blocks) {
+      PROF(c, "rope_kv", (double)T * (c->qd + 3.0 * c->kvd) * 8.0,
+           rope_kv_launch(c->qkv, nqkv, T, c->pos_d, c->seq_d, c->nh, c->nkv, c->hd, c->inv_freq_d, w.q_norm,
+                          w.k_norm, eps, kp, vp, c->page, c->bt_d, c->max_pages, st));
+      AttnArgs a{};
+      a.q = c->qkv; a.ldq = nqkv; a.T = T; a.pos = c->pos_d; a.seq = c->seq_d;
+      a.nh = c->nh; a.nkv = c->nkv; a.hd = c->hd;
+      a.kp = kp; a.vp = vp;
+      a.page = c->page; a.bt = c->bt_d; a.max_pages = c->max_pages;
+      a.qb_tok0 = c->qb_tok0_d; a.qb_len = c->qb_len_d;
+      a.nqb = nqb; a.qb_max = qb_max; a.nsplit = nsplit; a.part = c->part;
+      a.out32 = c->ao32; a.ldo = c->qd; a.outxs = nullptr;
+      PROF(c, "attention", kv_bytes_hint / c->cfg.layers + (double)T * c->qd * 8.0, attention_launch(a, st));
+    } else {
+      const AttnRope rope{c->inv_freq_d, w.q_norm, w.k_norm, eps, kp, vp};
+      PROF(c, "attention", kv_bytes_hint / c->cfg.layers + (double)T * c->qd * 8.0,
+           attention_decode_launch(c->qkv, nqkv, T, c->pos_d, c->seq_d, c->nh, c->nkv, c->hd, kp, vp, c->page,
+                                   c->bt_d, c->max_pages, nsplit, c->part, c->ticket_d, c->ao32, c->qd, nullptr, st,
+                                   &rope, (int64_t)(c->layer_kv / c->hd)));
+    }
+    Q8_TRY(rowpar("gemm_o", c->ao32, c->qd, w.o));
+    PROF(c, "rmsnorm", (double)T * H * (pending ? 16.0 : 8.0),
+         rmsnorm_launch(c->h, pending, w.post_norm, T, H, eps, c->xn32, nullptr, nullptr, st));
+    pending = nullptr;
+    PROF(c, "gemm_gateup", bytes(T, H, 2 * c->F),
+         gemm_bf16_launch(EPI_SWIGLU, c->xn32, H, T, H, bw(w.gu), c->F, c->act32, c->F, st));
+    Q8_TRY(rowpar("gemm_down", c->act32, c->F, w.down));
+  }
+  if (lrows <= 0) return Q8_OK;
+  float* hrow = c->h + (size_t)lrow0 * H;
+  const float* prow = pending ? pending + (size_t)lrow0 * H : nullptr;
+  PROF(c, "rmsnorm", (double)lrows * H * 8.0,
+       rmsnorm_launch(hrow, prow, c->final_norm, lrows, H, eps, c->xn32, nullptr, nullptr, st));
+  PROF(c, "gemm_lmhead", bytes(lrows, H, c->V_loc),
+       gemm_bf16_launch(EPI_STORE, c->xn32, H, lrows, H, bw(c->lm_head), c->V_loc, c->logits, c->V_loc, st));
+  return select_tokens(c, lrow0, lrows);
+}
+
 // Runs T tokens whose ids/pos/seq (and query blocks, when qb_tok0 != null) are
 // already in the device buffers.  Produces logits + argmax for token rows
 // [lrow0, lrow0 + lrows).  kv_ctx_hint bounds the context for split sizing.
@@ -354,6 +487,7 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
     PROF(c, "decode_step", c->dr_wbytes + kv_bytes_hint, ring_step(c, false));
     return Q8_OK;
   }
+  if (c->bf16) return run_tokens_bf16(c, T, blocks, nqb, qb_max, nsplit, lrow0, lrows, kv_bytes_hint);
   PROF(c, "embed", (double)T * (q8_row_bytes(H) + H * 4.0),
        embed_launch(c->embed, H, c->ids_d, T, c->h, st));
   const float* pending = nullptr;  // row-parallel partial sum not yet added to h
@@ -500,50 +634,7 @@ static int run_tokens(q8_ctx* c, int T, bool blocks, int nqb, int qb_max, int ns
          gemm_dispatch(EPI_STORE, c->xn32, H, c->xs_in, lrows, H, c->lm_head, c->V_loc, c->logits, c->V_loc, nullptr,
                        st));
   }
-  if (c->samp_temp > 0.f) {  // sampled tokens into argmax_d
-    cudaEvent_t pe;
-    Q8_TRY(prof_begin(c, &pe));
-    const float* lg = c->logits;
-    if (tp) {  // every rank samples the whole vocabulary with the same draws
-      ncclResult_t r = ncclAllGather(c->logits, c->lg_gather, (size_t)lrows * c->V_loc, ncclFloat, c->comm, st);
-      if (r != ncclSuccess) {
-        set_error("logits allgather: %s", ncclGetErrorString(r));
-        return Q8_ERR_COMM;
-      }
-      for (int k = 0; k < c->tp_size; ++k)  // [tp][rows][V_loc] -> [rows][V]
-        Q8_CUDA(cudaMemcpy2DAsync(c->samp_logits + (size_t)k * c->V_loc, (size_t)c->V * 4,
-                                  c->lg_gather + (size_t)k * lrows * c->V_loc, (size_t)c->V_loc * 4,
-                                  (size_t)c->V_loc * 4, lrows, cudaMemcpyDeviceToDevice, st));
-      lg = c->samp_logits;
-    }
-    k_sample_draws<<<ceil_div(lrows, 128), 128, 0, st>>>(c->pos_d + lrow0, c->seq_d + lrow0, lrows, c->samp_seed,
-                                                         c->samp_u);
-    Q8_TRY(launch_check("k_sample_draws"));
-    Q8_TRY(sample_launch(lg, lrows, c->V, c->V, c->samp_temp, c->samp_top_p, c->samp_u, c->argmax_d, c->samp_ws,
-                         c->samp_ws_bytes, st));
-    Q8_TRY(prof_end(c, "sample", (double)lrows * c->V * 4.0));
-  } else if (!tp) {
-    PROF(c, "argmax", (double)lrows * c->V * 4.0,
-         argmax_launch(c->logits, lrows, c->V, c->V, c->argmax_d, st));
-  } else {
-    cudaEvent_t pe;
-    Q8_TRY(prof_begin(c, &pe));
-    k_argmax_local<<<lrows, 1024, 0, st>>>(c->logits, c->V_loc, c->V_loc, c->am_val, c->am_idx);
-    Q8_TRY(launch_check("k_argmax_local"));
-    ncclGroupStart();
-    ncclAllGather(c->am_val, c->am_gval, lrows, ncclFloat, c->comm, st);
-    ncclAllGather(c->am_idx, c->am_gidx, lrows, ncclInt32, c->comm, st);
-    ncclResult_t r = ncclGroupEnd();
-    if (r != ncclSuccess) {
-      set_error("argmax allgather: %s", ncclGetErrorString(r));
-      return Q8_ERR_COMM;
-    }
-    k_argmax_pick<<<ceil_div(lrows, 128), 128, 0, st>>>(c->am_gval, c->am_gidx, c->tp_size, lrows, c->V_loc,
-                                                         c->argmax_d);
-    Q8_TRY(launch_check("k_argmax_pick"));
-    Q8_TRY(prof_end(c, "argmax", (double)lrows * c->V_loc * 4.0));
-  }
-  return Q8_OK;
+  return select_tokens(c, lrow0, lrows);
 }
 
 // Device status words (bounded waits of the ring step, the tensor-core GEMM,
@@ -765,6 +856,8 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
   Q8_CHECK_ARG(max_seqs >= 1 && maxlen >= 1 && max_tokens >= 1, "q8_create: bad capacities");
   Q8_CHECK_ARG(tp_size == 1 || nccl_id, "q8_create: tp_size > 1 needs an NCCL id");
   Q8_CHECK_ARG(C.n_heads / C.n_kv <= 64, "q8_create: GQA group > 64 unsupported");
+  Q8_CHECK_ARG(C.weight_dtype == 0 || C.weight_dtype == Q8_PACKED || C.weight_dtype == Q8_BF16,
+               "q8_create: weight_dtype must be Q8_PACKED (or 0) or Q8_BF16");
 
   q8_ctx* c = new q8_ctx();
   c->cfg = C;
@@ -782,10 +875,12 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
   c->qd = c->nh * c->hd;
   c->kvd = c->nkv * c->hd;
   c->F = C.inter / tp_size;
+  c->bf16 = C.weight_dtype == Q8_BF16;
   {
-    // Q8_TC=0 keeps prefill on the GEMV kernels (A/B comparisons)
+    // Q8_TC=0 keeps prefill on the GEMV kernels (A/B comparisons); the
+    // tensor-core GEMM reads packed Q8 rows only
     const char* e = getenv("Q8_TC");
-    c->tc = C.hidden % 512 == 0 && c->qd % 512 == 0 && c->F % 512 == 0 && !(e && e[0] == '0');
+    c->tc = !c->bf16 && C.hidden % 512 == 0 && c->qd % 512 == 0 && c->F % 512 == 0 && !(e && e[0] == '0');
     // Q8_TC_DECODE_MIN: decode batches from this many sequences use the
     // tensor-core pipeline (default 16; the GEMV kernels below it)
     const char* d = getenv("Q8_TC_DECODE_MIN");
@@ -830,16 +925,16 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
     off += bytes;
     return o;
   };
-  const size_t o_embed = take((size_t)C.vocab * q8_row_bytes(H));
-  const size_t o_head = C.tied ? 0 : take((size_t)c->V_loc * q8_row_bytes(H));
+  const size_t o_embed = take((size_t)C.vocab * wrow_bytes(c, H));
+  const size_t o_head = C.tied ? 0 : take((size_t)c->V_loc * wrow_bytes(c, H));
   const size_t o_fnorm = take((size_t)H * 2);
   struct LOff { size_t qkv, o, gu, down, inn, post, qn, kn; };
   std::vector<LOff> lo(C.layers);
   for (int L = 0; L < C.layers; ++L) {
-    lo[L].qkv = take((size_t)(c->qd + 2 * c->kvd) * q8_row_bytes(H));
-    lo[L].o = take((size_t)H * q8_row_bytes(c->qd));
-    lo[L].gu = take((size_t)2 * c->F * q8_row_bytes(H));
-    lo[L].down = take((size_t)H * q8_row_bytes(c->F));
+    lo[L].qkv = take((size_t)(c->qd + 2 * c->kvd) * wrow_bytes(c, H));
+    lo[L].o = take((size_t)H * wrow_bytes(c, c->qd));
+    lo[L].gu = take((size_t)2 * c->F * wrow_bytes(c, H));
+    lo[L].down = take((size_t)H * wrow_bytes(c, c->F));
     lo[L].inn = take((size_t)H * 2);
     lo[L].post = take((size_t)H * 2);
     lo[L].qn = C.qk_norm ? take((size_t)c->hd * 2) : 0;
@@ -849,7 +944,7 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
   int s;
   if ((s = dmalloc((void**)&c->warena, c->wbytes))) return bail(s);
   c->embed = c->warena + o_embed;
-  c->lm_head = C.tied ? c->embed + (size_t)c->V_off * q8_row_bytes(H) : c->warena + o_head;
+  c->lm_head = C.tied ? c->embed + (size_t)c->V_off * wrow_bytes(c, H) : c->warena + o_head;
   c->final_norm = (uint16_t*)(c->warena + o_fnorm);
   c->layers.resize(C.layers);
   for (int L = 0; L < C.layers; ++L) {
@@ -942,7 +1037,7 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
   {
     const char* e = getenv("Q8_RING");
     const char* why = nullptr;
-    if (!(e && e[0] == '0') && tp_size == 1 &&
+    if (!(e && e[0] == '0') && tp_size == 1 && !c->bf16 &&
         dr_supported(H, c->nh, c->nkv, c->hd, c->F, c->V, c->page, &why)) {
       if ((s = dr_prepare(c->hd, &c->dr_grid))) return bail(s);
     }
@@ -1138,8 +1233,19 @@ static int load_tensor_impl(q8_ctx* c, const char* cname, int dtype, int64_t row
       else if (p.slot == "gu") base = w.gu;
       else if (p.slot == "down") base = w.down;
     }
-    uint8_t* dst = base + p.dst_row * q8_row_bytes(p.kl);
-    s = put_packed(c, dst, src, p.m, p.row0, p.nrows, p.k0, p.kl, dtype, on_dev);
+    if (c->bf16) {  // bf16 rows stored as given (the slice of this rank)
+      if (dtype != Q8_BF16) {
+        set_error("tensor %s: a bf16-weight model (weight_dtype Q8_BF16) loads bf16 matrices, not packed Q8", cname);
+        return Q8_ERR_FORMAT;
+      }
+      uint8_t* dst = base + p.dst_row * p.kl * 2;
+      Q8_CUDA(cudaMemcpy2DAsync(dst, p.kl * 2, src + (p.row0 * p.m + p.k0) * 2, p.m * 2, p.kl * 2, p.nrows,
+                                on_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, c->st));
+      Q8_CUDA(cudaStreamSynchronize(c->st));
+    } else {
+      uint8_t* dst = base + p.dst_row * q8_row_bytes(p.kl);
+      s = put_packed(c, dst, src, p.m, p.row0, p.nrows, p.k0, p.kl, dtype, on_dev);
+    }
   }
   if (s == Q8_OK) c->loaded.insert(name);
   return s;

@@ -71,6 +71,19 @@ def mm_q8(x: torch.Tensor, packed: torch.Tensor, m: int, out: torch.Tensor = Non
     return y
 
 
+def mm_bf16(x: torch.Tensor, w_bf16: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
+    """y[s, n] = x[s, m] . W[n, m]^T with f32 x and plain bf16 W (mm_op,
+    src/llama_common.mojo:636-684)."""
+    _need_cuda(x, w_bf16)
+    assert x.dtype == torch.float32 and w_bf16.dtype == torch.bfloat16 and x.stride(1) == 1
+    assert w_bf16.is_contiguous() and x.shape[1] == w_bf16.shape[1]
+    s, m = x.shape
+    n = w_bf16.shape[0]
+    y = out if out is not None else torch.empty((s, n), dtype=torch.float32, device=x.device)
+    check(lib().q8op_gemm_bf16(_p(x), x.stride(0), s, m, _p(w_bf16), n, _p(y), y.stride(0), _stream(x)))
+    return y
+
+
 def mm_q8_swiglu(x: torch.Tensor, packed_gu: torch.Tensor, m: int) -> torch.Tensor:
     """silu(x.Wg^T) * (x.Wu^T) with the F gate rows then F up rows in ``packed_gu``."""
     _need_cuda(x, packed_gu)

@@ -148,6 +148,8 @@ class Config:
     orig_ctx: float = 8192.0
     qk_norm: bool = False          # Qwen3 per-head RMSNorm (llama_q8.mojo:171)
     tied: bool = True              # lm_head = embed_tokens (qwen_q8.mojo:143-145)
+    weights: str = "q8"            # "q8": packed Q8 matrices; "bf16": the non-Q8 path
+                                   # (run_layer / mm_op, src/llama_common.mojo:636-780)
 
     @property
     def q_dim(self):
@@ -230,18 +232,28 @@ def tensor_shape(cfg: Config, name: str):
             "gate_proj": (F, H), "up_proj": (F, H), "down_proj": (H, F)}[tail]
 
 
-def make_bf16_weights(cfg: Config, seed: int = 0, std: float = 0.02):
+def make_bf16_weights(cfg: Config, seed: int = 0, std: float = 0.02, norm_std: float = 0.0):
     """Seeded synthetic checkpoint: every 2-D tensor is N(0, std) f32 from
     ``default_rng(seed)`` drawn in ``weight_names`` order, rounded to bf16 (RNE);
-    norm weights are 1.0 (HF init).  Yields (name, bf16 uint16 array)."""
+    norm weights are 1.0 (HF init), or 1 + N(0, norm_std) drawn in the same
+    stream when ``norm_std`` > 0.  Yields (name, bf16 uint16 array)."""
     rng = np.random.default_rng(seed)
     for name in weight_names(cfg):
         shp = tensor_shape(cfg, name)
         if len(shp) == 1:
-            yield name, bf16_round(np.ones(shp, np.float32))
+            v = np.ones(shp, np.float32)
+            if norm_std > 0:
+                v = v + rng.standard_normal(shp, dtype=np.float32) * np.float32(norm_std)
+            yield name, bf16_round(v)
         else:
             w = rng.standard_normal(shp, dtype=np.float32) * np.float32(std)
             yield name, bf16_round(w)
+
+
+def make_bf16_checkpoint(cfg: Config, seed: int = 0, std: float = 0.02,
+                         norm_std: float = 0.0) -> Dict[str, np.ndarray]:
+    """The synthetic checkpoint as stored for the bf16 path: every tensor bf16 bits."""
+    return dict(make_bf16_weights(cfg, seed, std, norm_std))
 
 
 def make_q8_checkpoint(cfg: Config, seed: int = 0, std: float = 0.02) -> Dict[str, np.ndarray]:
@@ -326,7 +338,9 @@ class OracleModel:
     Mirrors the reference model shell API: ``forward(ids) -> logits``,
     ``forward_argmax(ids) -> int``, ``n_cached`` (qwen3_mojo/src/qwen_q8.mojo:126-162).
     Weights are dequantized once (``q * f32(scale)``) so the matmuls are the
-    reference f32 path on Q8 weights.
+    reference f32 path on Q8 weights.  With ``cfg.weights == "bf16"`` every
+    tensor is bf16 bits widened to f32 (the reference's bf16 shells,
+    src/llama_gpu.mojo:103-155 over run_layer, src/llama_common.mojo:697-780).
     """
 
     def __init__(self, cfg: Config, ckpt: Dict[str, np.ndarray], maxlen: int = 1 << 30):
@@ -344,7 +358,10 @@ class OracleModel:
         if name not in self._w:
             a = self._ck[name]
             shp = tensor_shape(self.cfg, name)
-            self._w[name] = bf16_to_f32(a) if len(shp) == 1 else dequant_q8(a, shp[1])
+            if len(shp) == 1 or self.cfg.weights == "bf16":
+                self._w[name] = bf16_to_f32(a).reshape(shp)
+            else:
+                self._w[name] = dequant_q8(a, shp[1])
         return self._w[name]
 
     def reset(self):
@@ -382,7 +399,10 @@ class OracleModel:
         s = len(ids)
         if self.n_cached + s > self.maxlen:
             raise RuntimeError("KV cache full")  # qwen_q8.mojo:128-129
-        x = embed_q8(self._ck["model.embed_tokens.weight"], c.hidden, ids)
+        if c.weights == "bf16":  # k_embed_gather (src/llama_common.mojo:183-194)
+            x = bf16_to_f32(np.asarray(self._ck["model.embed_tokens.weight"])[np.asarray(ids, np.int64)])
+        else:
+            x = embed_q8(self._ck["model.embed_tokens.weight"], c.hidden, ids)
         pos = self.n_cached
         for L in range(c.layers):
             x = self.layer(x, L, pos)

@@ -26,6 +26,14 @@ config and ``W`` / ``load_w`` are replaced by the synthetic weights.
 
 ``--big`` adds config[0] (Llama-3.2-1B dims, seed 0, 16-token prompt from
 seed 1): reference prefill outputs plus 32 greedy decode steps of the oracle.
+
+bf16 weights (the reference's non-Q8 path): the same two reference scripts
+with ``W`` / ``load_w`` returning the bf16 checkpoint widened to f32 — which
+is what they compute on a real bf16 checkpoint — over seeded checkpoints
+whose norm weights are 1 + N(0, 0.1):
+``scripts/gen_oracle.py:layer`` on tiny-llama -> tiny_llama_bf16_prefill.npz,
+``qwen3_mojo/scripts/bench_python.py:forward`` on tiny-qwen3 ->
+tiny_qwen3_bf16_decode.npz.  ``--bf16-only`` writes just these two.
 """
 from __future__ import annotations
 
@@ -116,7 +124,10 @@ def make_W(cfg: O.Config, ck: dict):
         if name not in cache:
             shp = O.tensor_shape(cfg, name)
             a = ck[name]
-            cache[name] = O.bf16_to_f32(a).reshape(shp) if len(shp) == 1 else O.dequant_q8(a, shp[1])
+            if len(shp) == 1 or cfg.weights == "bf16":
+                cache[name] = O.bf16_to_f32(a).reshape(shp)
+            else:
+                cache[name] = O.dequant_q8(a, shp[1])
         return cache[name].copy()
     return W
 
@@ -196,16 +207,38 @@ def pack_cases(pack_q8) -> dict:
     return cases
 
 
+# --------------------------------------------------------------------------- bf16 path
+
+def bf16_fixtures(ref: str, scratch: str):
+    """Reference outputs on bf16 weights (the checkpoint as stored, no packing)."""
+    cfg = O.PRESETS["tiny-llama"].replace(weights="bf16")
+    ck = O.make_bf16_checkpoint(cfg, seed=5, norm_std=0.1)
+    ns = exec_ref_script(ref, "scripts/gen_oracle.py", os.path.join(scratch, "llama32bf"))
+    set_llama_consts(ns, cfg)
+    np.savez_compressed(os.path.join(HERE, "tiny_llama_bf16_prefill.npz"),
+                        **ref_prefill(ns, cfg, ck, O.random_ids(cfg, 11), "model.embed_tokens.weight"))
+    cfg = O.PRESETS["tiny-qwen3"].replace(weights="bf16")
+    ck = O.make_bf16_checkpoint(cfg, seed=6, norm_std=0.1)
+    nsb = exec_ref_script(ref, "qwen3_mojo/scripts/bench_python.py", os.path.join(scratch, "qwen3bf"))
+    np.savez_compressed(os.path.join(HERE, "tiny_qwen3_bf16_decode.npz"),
+                        **ref_cached_decode_qwen(nsb, cfg, ck, O.random_ids(cfg, 7), 6))
+
+
 # --------------------------------------------------------------------------- main
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True)
     ap.add_argument("--big", action="store_true")
+    ap.add_argument("--bf16-only", action="store_true")
     a = ap.parse_args()
     ref = a.ref
     pack_q8 = load_pack_q8(ref)
     scratch = tempfile.mkdtemp(prefix="q8golden_")
+    if a.bf16_only:
+        bf16_fixtures(ref, scratch)
+        print("wrote bf16 fixtures to", HERE)
+        return
 
     np.savez_compressed(os.path.join(HERE, "pack_cases.npz"), **pack_cases(pack_q8))
 
@@ -240,6 +273,8 @@ def main():
     nsb = exec_ref_script(ref, "qwen3_mojo/scripts/bench_python.py", os.path.join(scratch, "qwen3b"))
     np.savez_compressed(os.path.join(HERE, "tiny_qwen3_decode.npz"),
                         **ref_cached_decode_qwen(nsb, cfg, ck, O.random_ids(cfg, 7), 6))
+
+    bf16_fixtures(ref, scratch)
 
     if a.big:
         # --- config[0]: Llama-3.2-1B dims, 16-token prompt, 32 greedy steps

@@ -23,7 +23,7 @@ def _free_port():
     return p
 
 
-def _rank(rank, world, port, cfgname, ids, steps, q):
+def _rank(rank, world, port, cfgname, ids, steps, q, weights="q8"):
     import datetime
 
     import torch.distributed as dist
@@ -36,7 +36,7 @@ def _rank(rank, world, port, cfgname, ids, steps, q):
     try:
         uid = [nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
-        m = Q8Model(PRESETS[cfgname], device=rank, maxlen=64, max_seqs=2, tp_rank=rank, tp_size=world,
+        m = Q8Model(PRESETS[cfgname].replace(weights=weights), device=rank, maxlen=64, max_seqs=2, tp_rank=rank, tp_size=world,
                     nccl_id=uid[0])
         for name, w in O.make_bf16_weights(O.PRESETS[cfgname], 0):
             m.load_tensor(name, w, packed=False)
@@ -62,12 +62,12 @@ def _rank(rank, world, port, cfgname, ids, steps, q):
         dist.destroy_process_group()
 
 
-def _run_tp2(cfgname, ids):
+def _run_tp2(cfgname, ids, weights="q8"):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, cfgname, ids, 4, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, cfgname, ids, 4, q, weights)) for r in range(2)]
     for p in procs:
         p.start()
     try:
@@ -81,14 +81,15 @@ def _run_tp2(cfgname, ids):
     return out
 
 
-@pytest.mark.parametrize("cfgname", ["tiny-llama", "tiny-qwen3", "tiny-llama-untied"])
-def test_tp2_matches_oracle(cuda, cfgname):
+@pytest.mark.parametrize("cfgname,weights", [("tiny-llama", "q8"), ("tiny-qwen3", "q8"), ("tiny-llama-untied", "q8"),
+                                             ("tiny-llama-untied", "bf16")])
+def test_tp2_matches_oracle(cuda, cfgname, weights):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    ocfg = O.PRESETS[cfgname]
+    ocfg = O.PRESETS[cfgname].replace(weights=weights)
     ids = O.random_ids(ocfg, 9, seed=41)
-    out = _run_tp2(cfgname, ids)
-    ck = O.make_q8_checkpoint(ocfg)
+    out = _run_tp2(cfgname, ids, weights)
+    ck = O.make_q8_checkpoint(ocfg) if weights == "q8" else O.make_bf16_checkpoint(ocfg)
     orc = O.OracleModel(ocfg, ck)
     ref = orc.forward(ids)
     assert O.rel_l2(out["hidden1"], orc.trace["after_layer1"]) < 1e-5

@@ -179,3 +179,27 @@ def test_c_whole_model_matches_pinned_oracle(cfgname):
         t_ref = orc.forward_argmax([t_ref])
         t_c = int(np.argmax(rm.token(t_c)))
         assert t_ref == t_c
+
+
+def test_bf16_prefill_matches_reference_gen_oracle(golden_dir):
+    """bf16 weights (the non-Q8 path): gen_oracle.layer over the checkpoint
+    widened to f32, norm weights 1 + N(0, 0.1)."""
+    g = _load(golden_dir, "tiny_llama_bf16_prefill.npz")
+    cfg = O.PRESETS["tiny-llama"].replace(weights="bf16")
+    m = O.OracleModel(cfg, O.make_bf16_checkpoint(cfg, seed=5, norm_std=0.1))
+    lg = m.forward(list(g["ids"]))
+    for L in (0, 1):
+        np.testing.assert_allclose(m.trace[f"after_layer{L}"], g[f"after_layer{L}"], rtol=0, atol=1e-6)
+    np.testing.assert_allclose(lg, g["last_logits"], rtol=0, atol=1e-6)
+
+
+def test_bf16_cached_decode_matches_reference_bench_python(golden_dir):
+    g = _load(golden_dir, "tiny_qwen3_bf16_decode.npz")
+    cfg = O.PRESETS["tiny-qwen3"].replace(weights="bf16")
+    m = O.OracleModel(cfg, O.make_bf16_checkpoint(cfg, seed=6, norm_std=0.1))
+    lg = [m.forward(list(g["ids"]))]
+    for t in g["tokens"][:-1]:
+        lg.append(m.forward([int(t)]))
+    lg = np.stack(lg)
+    assert O.rel_l2(lg, g["logits"]) < 1e-5
+    assert [int(np.argmax(x)) for x in lg] == g["tokens"].tolist()
