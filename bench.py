@@ -332,11 +332,15 @@ def main():
     step_ms_prof = sum(v[0] for k, v in agg.items() if not k.startswith("phase:")) / nprof
     breakdown = {k: {"ms_per_step": round(v[0] / nprof, 4), "launches_per_step": v[2] // nprof,
                      "GB_s": round(v[1] / (v[0] / 1e3) / 1e9, 1) if v[0] > 0 else None} for k, v in agg.items()}
+    # DRAM traffic per launch of the dominant kernel: the ncu capture's
+    # traffic / algorithmic ratio (profiles/decode_traffic.json) times this
+    # launch's algorithmic bytes; null where no capture covers the kernel
     traffic = None
-    tp = os.path.join(REPO, "profiles", "gemv_traffic.json")
-    if os.path.exists(tp):
-        tj = json.load(open(tp))
-        traffic = tj.get(f"{a.model}/tp{world}/b{B}")
+    tp = os.path.join(REPO, "profiles", "decode_traffic.json")
+    if dom == ["decode_step"] and g_l > 0 and os.path.exists(tp):
+        ratio = json.load(open(tp)).get("k_decode_ring")
+        if ratio:
+            traffic = round(ratio * g_b / g_l)
 
     # launches per step: our kernels inside the generate graph = the profiled
     # decode launches + the on-device step epilogue (k_step_end), which the
