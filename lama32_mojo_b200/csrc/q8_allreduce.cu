@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(256) k_ar_p2p(ArArgs a) {
 }
 
 // ------------------------------------------------------------------ host side
-// block: [land 2*tp*slot floats][flag 2*tp*AR_NB ints][seq][ticket][status]
+// block: [land 2*tp*slot floats][flag 2*tp*AR_NB ints][seq][ticket][status] (256 B)[rx]
 static size_t ar_land_bytes(int tp, int64_t slot) { return ((size_t)2 * tp * slot * 4 + 255) & ~(size_t)255; }
 
 // Two collectives, taken by every rank whatever happens locally: an
@@ -117,7 +117,7 @@ struct ArHandleRec {
   int pad[15];
 };
 
-int ar_setup(ArState* s, ncclComm_t comm, int tp, int rank, int64_t max_floats, cudaStream_t st) {
+int ar_setup(ArState* s, ncclComm_t comm, int tp, int rank, int64_t max_floats, size_t rx_bytes, cudaStream_t st) {
   *s = ArState{};
   if (tp < 2 || tp > AR_MAXTP) return Q8_OK;
   s->tp = tp;
@@ -125,7 +125,8 @@ int ar_setup(ArState* s, ncclComm_t comm, int tp, int rank, int64_t max_floats, 
   s->slot = (max_floats + 63) & ~(int64_t)63;
   const size_t lb = ar_land_bytes(tp, s->slot);
   const size_t fb = (size_t)2 * tp * AR_NB * 4;
-  s->bytes = lb + fb + 256;
+  const size_t rxo = lb + fb + 256;  // the exchange block of the decode step, 256-byte aligned
+  s->bytes = rxo + ((rx_bytes + 255) & ~(size_t)255);
   ArHandleRec mine{};
   // zeroed on `st`, ahead of this rank's contribution to the exchange below
   if (cudaMalloc(&s->block, s->bytes) == cudaSuccess && cudaMemsetAsync(s->block, 0, s->bytes, st) == cudaSuccess &&
@@ -162,6 +163,7 @@ int ar_setup(ArState* s, ncclComm_t comm, int tp, int rank, int64_t max_floats, 
       }
       s->peers.land[k] = reinterpret_cast<float*>(p);
       s->peers.flag[k] = reinterpret_cast<int*>(p + lb);
+      s->peers.rx[k] = rx_bytes ? p + rxo : nullptr;
     }
   }
   // agree: P2P only if every rank mapped every peer
@@ -186,6 +188,8 @@ int ar_setup(ArState* s, ncclComm_t comm, int tp, int rank, int64_t max_floats, 
   s->seq = reinterpret_cast<int*>(base + lb + fb);
   s->ticket = s->seq + 1;
   s->status = s->seq + 2;
+  s->rx = rx_bytes ? base + rxo : nullptr;
+  s->rx_bytes = rx_bytes;
   s->ok = true;
   return Q8_OK;
 }

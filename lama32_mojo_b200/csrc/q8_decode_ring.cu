@@ -60,9 +60,24 @@
 // acquire ticket) merges the splits in order.  Every sum has a fixed order:
 // results do not depend on timing.
 //
-// Every wait is bounded (about a second): a wait that gives up sets the
-// device status word, after which every other wait returns at once and the
-// host reports Q8_ERR_TIMEOUT.  No load uses cluster multicast.
+// Tensor parallelism.  Each rank runs the step on its shards (column-parallel
+// q|k|v and gate|up rows, its kv heads, row-parallel K slices of o_proj and
+// down_proj, its vocabulary rows).  The row-parallel phases end in an
+// exchange inside the launch instead of a grid barrier: every CTA stores its
+// partial rows into every rank's inbox (plain stores into peer memory mapped
+// with CUDA IPC: no remote loads, no bulk copies from peers) and, after a CTA
+// barrier, counts itself on every rank's arrival counter with one
+// system-scope release per rank (cumulative over the CTA's stores); the next
+// phase's staging waits (acquire) for the CTAs of all ranks and adds the
+// partials in rank order, so every rank computes the same residual.  The
+// lm_head phase ends with the ranks' argmax keys maxed into every rank's slot.
+// Counters only grow: a step's targets derive from the rank's completed-step
+// count, so no rank ever resets memory another rank may be counting into.
+//
+// Every wait is bounded (seconds): a wait that gives up sets the device
+// status word, after which every other wait returns at once and the host
+// reports Q8_ERR_TIMEOUT (Q8_ERR_COMM for a tensor-parallel peer that never
+// arrived).  No load uses cluster multicast.
 #include "q8_decode_ring.h"
 #include "q8_kernels.h"
 
@@ -93,8 +108,10 @@ __device__ __forceinline__ void dr_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Bounded mbarrier wait: gives up after ~2^31 cycles (setting the status
-// word) or as soon as another wait has given up (checked every 2^10 polls).
+// Bounded mbarrier wait: gives up after ~2^34 cycles (~9 s, setting the
+// status word) or as soon as another wait has given up (checked every 2^10
+// polls).  The local bounds exceed the cross-rank exchange's (~2^33), so a
+// rank that never arrives is reported as such.
 __device__ __forceinline__ bool dr_mwait(uint64_t* bar, uint32_t parity, int* status) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
@@ -102,7 +119,7 @@ __device__ __forceinline__ bool dr_mwait(uint64_t* bar, uint32_t parity, int* st
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 0x3FFu) == 0) {
       if (dr_ld_volatile(status)) return false;
-      if (clock64() - t0 > (1ll << 31)) {
+      if (clock64() - t0 > (1ll << 34)) {
         atomicExch(status, Q8_ERR_TIMEOUT);
         return false;
       }
@@ -118,7 +135,7 @@ __device__ __forceinline__ void dr_grid_wait(const DrParams& P, unsigned int tar
     for (unsigned it = 1; dr_ld_acquire(P.bar) < target; ++it) {
       if ((it & 63u) == 0) {
         if (dr_ld_volatile(P.status)) break;
-        if (clock64() - t0 > (1ll << 31)) {
+        if (clock64() - t0 > (1ll << 34)) {
           atomicExch(P.status, Q8_ERR_TIMEOUT);
           break;
         }
@@ -126,6 +143,48 @@ __device__ __forceinline__ void dr_grid_wait(const DrParams& P, unsigned int tar
     }
   }
   dr_csync();
+}
+
+// Cross-rank exchange (tensor parallelism): wait until this rank's counter
+// `ctr` holds `target` arrivals of all ranks' CTAs (system-scope acquire).  The
+// bound is longer than the grid barrier's: the ranks' launches may be skewed
+// by their hosts.
+__device__ __forceinline__ unsigned long long dr_ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void dr_xwait1(const DrParams& P, const unsigned long long* ctr, unsigned long long target) {
+  if (dr_ld_volatile(P.status)) return;
+  const long long t0 = clock64();
+  for (unsigned it = 1; dr_ld_acquire_sys(ctr) < target; ++it) {
+    if ((it & 63u) == 0) {
+      if (dr_ld_volatile(P.status)) return;
+      if (clock64() - t0 > (1ll << 33)) {
+        atomicExch(P.status, Q8_ERR_COMM);
+        return;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void dr_xwait(const DrParams& P, const unsigned long long* ctr, unsigned long long target) {
+  if (threadIdx.x == 0) dr_xwait1(P, ctr, target);
+  dr_csync();
+}
+// This CTA's arrival on every rank's counter `k` after the consumer threads'
+// stores into the ranks' inboxes: the CTA barrier orders every thread's
+// stores before the arriving threads, whose system-scope release increments
+// are cumulative over what they observed (one release per rank instead of a
+// system fence in every thread).
+__device__ __forceinline__ void dr_xarrive(const DrParams& P, int k) {
+  dr_csync();
+  if (threadIdx.x < DR_MAXTP) {
+    unsigned long long* ctr = nullptr;
+#pragma unroll
+    for (int r = 0; r < DR_MAXTP; ++r)  // static indices into the parameter arrays
+      if (threadIdx.x == r && r < P.tp) ctr = P.xcnt[r];
+    if (ctr) asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(ctr + k) : "memory");
+  }
 }
 
 // Every consumer thread's stores of the phase (ordered before thread 0 by the
@@ -188,9 +247,9 @@ __device__ __forceinline__ DrG dr_gemv_desc(const DrParams& P, int kind, int L) 
   d.split = 0;
   switch (kind) {
     case DP_QKV: d.W = ly->qkv; d.K = P.H; N = P.nqkv; break;
-    case DP_O: d.W = ly->o; d.K = P.qd; N = P.H; break;
+    case DP_O: d.W = ly->o; d.K = P.qdp; N = P.H; break;
     case DP_GU: d.W = ly->gu; d.K = P.H; N = P.F; d.F2 = P.F; break;
-    case DP_DOWN: d.W = ly->down; d.K = P.F; N = P.H; d.split = 1; break;
+    case DP_DOWN: d.W = ly->down; d.K = P.Fp; N = P.H; d.split = 1; break;
     default: d.W = P.lm_head; d.K = P.H; N = P.V; break;
   }
   d.T = d.F2 ? N / 8 : N / 16;
@@ -352,8 +411,9 @@ enum { DS_F32 = 0, DS_EMBED = 1, DS_FOLD = 2 };
 
 // 16 values x[k0 .. k0+15] of the phase's input vector; every load of the
 // item is in flight before the first is used.
-template <int KIND>
-__device__ __forceinline__ void dr_load16(const DrParams& P, const float* src, int k0, float (&v)[16]) {
+template <int KIND, bool XP>
+__device__ __forceinline__ void dr_load16(const DrParams& P, const float* src, const float* slots, int nslots, int k0,
+                                          float (&v)[16]) {
   if constexpr (KIND == DS_EMBED) {
     const int64_t rb = (int64_t)P.H + P.H / 32;
     const uint8_t* row = P.embed + (int64_t)P.ids[0] * rb;
@@ -368,20 +428,41 @@ __device__ __forceinline__ void dr_load16(const DrParams& P, const float* src, i
   float4 a[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) a[i] = __ldcg(reinterpret_cast<const float4*>(src + k0) + i);
-  if constexpr (KIND == DS_FOLD) {  // residual + the down partial slots, in slot order
+  if constexpr (KIND == DS_FOLD && !XP) {  // + this GPU's partial slots (<= DR_NS, stride H), in slot order
     float4 pp[DR_NS][4];
 #pragma unroll
     for (int sl = 0; sl < DR_NS; ++sl)
 #pragma unroll
       for (int i = 0; i < 4; ++i)
-        pp[sl][i] = sl < P.nsf ? __ldcg(reinterpret_cast<const float4*>(P.pres + (int64_t)sl * P.H + k0) + i)
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        pp[sl][i] = sl < nslots ? __ldcg(reinterpret_cast<const float4*>(slots + (int64_t)sl * P.H + k0) + i)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int sl = 0; sl < DR_NS; ++sl) {
-      if (sl < P.nsf) {
+      if (sl < nslots) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           a[i].x += pp[sl][i].x; a[i].y += pp[sl][i].y; a[i].z += pp[sl][i].z; a[i].w += pp[sl][i].w;
+        }
+      }
+    }
+  }
+  if constexpr (KIND == DS_FOLD && XP) {  // + every rank's partial slots (stride H), in rank and slot order
+    for (int s0 = 0; s0 < nslots; s0 += DR_NS) {
+      float4 pp[DR_NS][4];
+#pragma unroll
+      for (int sl = 0; sl < DR_NS; ++sl)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          pp[sl][i] = s0 + sl < nslots
+                          ? __ldcg(reinterpret_cast<const float4*>(slots + (int64_t)(s0 + sl) * P.H + k0) + i)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int sl = 0; sl < DR_NS; ++sl) {
+        if (s0 + sl < nslots) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            a[i].x += pp[sl][i].x; a[i].y += pp[sl][i].y; a[i].z += pp[sl][i].z; a[i].w += pp[sl][i].w;
+          }
         }
       }
     }
@@ -393,13 +474,15 @@ __device__ __forceinline__ void dr_load16(const DrParams& P, const float* src, i
   }
 }
 
-// Stages the K inputs of a GEMV phase as digits: waits for the previous
-// phase of the grid (target arrivals; 0: none), then x from `kind`; with nw
-// (K <= 16 x 256), x = nw * x / sqrt(mean(x^2) + eps), the norm weights read
-// before the wait; with wb, this CTA's slice of the raw x is written back
-// (the residual of the layer).
-template <int KIND, bool RMS>
-__device__ void dr_stage(const DrParams& P, int ph, unsigned int target, int K, const float* src,
+// Stages the K inputs of a GEMV phase as digits (zero digits up to Kd): waits
+// for the previous phase of the grid (target arrivals; 0: none) or, with xc,
+// for `xtarget` arrivals of all ranks on that exchange counter; then x from
+// `kind` (DS_FOLD: src + nslots partial slots); with nw (K <= 16 x 256),
+// x = nw * x / sqrt(mean(x^2) + eps), the norm weights read before the wait;
+// with wb, this CTA's slice of the raw x is written back (the residual).
+template <int KIND, bool RMS, bool XP>
+__device__ void dr_stage(const DrParams& P, int ph, unsigned int target, const unsigned long long* xc,
+                         unsigned long long xtarget, int Kd, int K, const float* src, const float* slots, int nslots,
                          const uint16_t* nw, float* wb, uint8_t* xq, float4* fcol, float* scr) {
   constexpr int NT = DR_CW * 32;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, sq = lane & 3;
@@ -412,12 +495,13 @@ __device__ void dr_stage(const DrParams& P, int ph, unsigned int target, int K, 
       w0 = __ldg(reinterpret_cast<const uint4*>(nw + k0));
       w1 = __ldg(reinterpret_cast<const uint4*>(nw + k0 + 8));
     }
-    if (target) dr_grid_wait(P, target);
+    if (xc) dr_xwait(P, xc, xtarget);
+    else if (target) dr_grid_wait(P, target);
     dr_mark(P, ph, 0);
     float v[16];
     float ss = 0.f;
     if (valid) {
-      dr_load16<KIND>(P, src, k0, v);
+      dr_load16<KIND, XP>(P, src, slots, nslots, k0, v);
 #pragma unroll
       for (int i = 0; i < 16; ++i) ss = fmaf(v[i], v[i], ss);
       if (wb) {
@@ -448,22 +532,24 @@ __device__ void dr_stage(const DrParams& P, int ph, unsigned int target, int K, 
     }
     dr_digits16(v, valid, valid ? tid >> 2 : 0, sq, xq, fcol);
   } else {
-    if (target) dr_grid_wait(P, target);
+    if (xc) dr_xwait(P, xc, xtarget);
+    else if (target) dr_grid_wait(P, target);
     dr_mark(P, ph, 0);
     constexpr int R = 2;  // rounds whose loads are in flight together
-    for (int base = 0; base < nitem; base += R * NT) {
+    const int nitem_d = Kd / 16;  // with the zero padding
+    for (int base = 0; base < nitem_d; base += R * NT) {
       float v[R][16];
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         const int item = base + r * NT + tid;
-        if (item < nitem) dr_load16<KIND>(P, src, item * 16, v[r]);
+        if (item < nitem) dr_load16<KIND, XP>(P, src, slots, nslots, item * 16, v[r]);
       }
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         const int item = base + r * NT + tid;
-        if (base + r * NT < nitem) {
-          const bool valid = item < nitem;
-          if (!valid) {
+        if (base + r * NT < nitem_d) {
+          const bool valid = item < nitem_d;
+          if (!valid || item >= nitem) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) v[r][i] = 0.f;
           }
@@ -877,7 +963,7 @@ __device__ void dr_attn(const DrParams& P, int L, uint8_t* ring, uint64_t* full,
 }
 
 // ------------------------------------------------------------------ the step
-template <int HD>
+template <int HD, bool XP>
 __global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -893,6 +979,7 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P)
   __shared__ float sm_m[DR_CW][DR_GMAX], sm_l[DR_CW][DR_GMAX];
   __shared__ int s_last;
   __shared__ unsigned long long s_key[DR_CW];
+  __shared__ unsigned long long s_epoch;  // completed steps of this rank (tensor parallel)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == DR_CW * 32) {
@@ -910,6 +997,14 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P)
 
   // ---------------------------------------------------------------- consumers
   const int G = gridDim.x, c = blockIdx.x;
+  constexpr bool tp = XP;  // tensor-parallel instantiation
+  // exchange targets grow across steps: the counters are never reset (a rank
+  // may already count into a peer's counter for its next step before that
+  // peer's launch begins)
+  if constexpr (XP) {
+    if (threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile unsigned long long*>(P.xstep);
+    dr_csync();
+  }
   int u = 0;
   unsigned int target = 0;
   const int nphase = 5 * P.L + 1;
@@ -931,19 +1026,45 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P)
     float* hc = (L & 1) ? P.h1 : P.h0;  // this layer's residual
     float* hp = (L & 1) ? P.h0 : P.h1;  // the previous layer's
     // the stagings wait for the previous phase (after their static loads);
-    // mark 0 is then the end of the wait
+    // mark 0 is then the end of the wait.  Folds: the residual + the previous
+    // down_proj's partials (this GPU's slots, or every rank's, in rank order)
+    const int Lp = (kind == DP_LM ? P.L : L) - 1;
+    const float* dslots = tp ? P.xin_me + dr_xin_region(Lp & 1, 1, P.tp, P.H) : P.pres;
+    const int dn = tp ? P.tp * P.nsf : P.nsf;
+    const unsigned long long* dxc = tp ? P.xcnt_me + 1 : nullptr;
+    const unsigned long long dxt = (s_epoch * (unsigned long long)P.L + (unsigned long long)Lp + 1) *
+                                   (unsigned long long)P.gsum;
     switch (kind) {
       case DP_QKV:
-        if (L == 0) dr_stage<DS_EMBED, true>(P, ph, target, P.H, hp, ly->in_norm, hc, xq, fcol, scr);
-        else dr_stage<DS_FOLD, true>(P, ph, target, P.H, hp, ly->in_norm, hc, xq, fcol, scr);
+        if (L == 0)
+          dr_stage<DS_EMBED, true, XP>(P, ph, target, nullptr, 0, P.H, P.H, hp, nullptr, 0, ly->in_norm, hc, xq, fcol,
+                                   scr);
+        else
+          dr_stage<DS_FOLD, true, XP>(P, ph, target, dxc, dxt, P.H, P.H, tp ? P.hm : hp, dslots, dn, ly->in_norm, hc, xq,
+                                  fcol, scr);
         break;
-      case DP_O: dr_stage<DS_F32, false>(P, ph, target, P.qd, P.ao, nullptr, nullptr, xq, fcol, scr); break;
-      case DP_GU: dr_stage<DS_F32, true>(P, ph, target, P.H, hc, ly->post_norm, nullptr, xq, fcol, scr); break;
-      case DP_DOWN: dr_stage<DS_F32, false>(P, ph, target, P.F, P.act, nullptr, nullptr, xq, fcol, scr); break;
-      default: {
-        const int Lp = P.L - 1;
-        dr_stage<DS_FOLD, true>(P, ph, target, P.H, (Lp & 1) ? P.h1 : P.h0, P.final_norm, nullptr, xq, fcol, scr);
-      }
+      case DP_O:
+        dr_stage<DS_F32, false, XP>(P, ph, target, nullptr, 0, P.qdp, P.qd, P.ao, nullptr, 0, nullptr, nullptr, xq, fcol,
+                                scr);
+        break;
+      case DP_GU:
+        if constexpr (XP)  // + every rank's o_proj partial; the sum is kept as the mid residual
+          dr_stage<DS_FOLD, true, XP>(P, ph, target, P.xcnt_me + 0,
+                                      (s_epoch * (unsigned long long)P.L + (unsigned long long)L + 1) *
+                                          (unsigned long long)P.gsum,
+                                      P.H, P.H, hc, P.xin_me + dr_xin_region(L & 1, 0, P.tp, P.H), P.tp,
+                                      ly->post_norm, P.hm, xq, fcol, scr);
+        else
+          dr_stage<DS_F32, true, XP>(P, ph, target, nullptr, 0, P.H, P.H, hc, nullptr, 0, ly->post_norm, nullptr, xq,
+                                     fcol, scr);
+        break;
+      case DP_DOWN:
+        dr_stage<DS_F32, false, XP>(P, ph, target, nullptr, 0, P.Fp, P.F, P.act, nullptr, 0, nullptr, nullptr, xq, fcol,
+                                scr);
+        break;
+      default:
+        dr_stage<DS_FOLD, true, XP>(P, ph, target, dxc, dxt, P.H, P.H, tp ? P.hm : ((Lp & 1) ? P.h1 : P.h0), dslots, dn,
+                                P.final_norm, nullptr, xq, fcol, scr);
     }
     float* red = reinterpret_cast<float*>(xq + (((size_t)d.K * 3 + 15) & ~(size_t)15));
     dr_mark(P, ph, 1);
@@ -969,7 +1090,7 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P)
         const int row = (t_lo + lt) * 16 + r;
         const float v = dr_tile_sum(d, red, lt, r);
         P.logits[row] = v;
-        const unsigned long long k = dr_key(v, row);
+        const unsigned long long k = dr_key(v, P.V_off + row);
         best = k > best ? k : best;
       }
 #pragma unroll
@@ -989,7 +1110,23 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P)
                      : "l"(P.lm_ticket)
                      : "memory");
         if (old == G - 1) {  // every CTA's maximum is in: the step's token
-          const unsigned long long k = atomicAdd(P.amax, 0ull);
+          unsigned long long k = atomicAdd(P.amax, 0ull);
+          if (tp) {  // the ranks' maxima: into every rank's slot of this step, then count
+            const unsigned long long epoch = s_epoch;
+            const int sl = (int)(epoch & 1ull);
+#pragma unroll
+            for (int r = 0; r < DR_MAXTP; ++r)
+              if (r < P.tp) atomicMax_system(P.xamax[r] + sl, k);
+            __threadfence_system();
+#pragma unroll
+            for (int r = 0; r < DR_MAXTP; ++r)
+              if (r < P.tp) asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(P.xcnt[r] + 2) : "memory");
+            dr_xwait1(P, P.xcnt_me + 2, (epoch + 1ull) * (unsigned long long)P.tp);
+            k = dr_ld_acquire_sys(P.xamax_me + sl);
+            // every rank's key of this step is in: the slot is free for step + 2
+            P.xamax_me[sl] = 0ull;
+            *reinterpret_cast<volatile unsigned long long*>(P.xstep) = epoch + 1ull;
+          }
           const int32_t tok = (int32_t)(~(uint32_t)(k & 0xFFFFFFFFull));
           P.argmax[0] = tok;
           if (P.gen) {
@@ -1013,17 +1150,37 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P)
         if (kind == DP_QKV) {
           P.qkv[row] = v;
         } else if (kind == DP_O) {
-          hc[row] = __ldcg(hc + row) + v;
+          if (tp) {  // this rank's partial row into every rank's inbox
+            const int64_t off = dr_xin_region(L & 1, 0, P.tp, P.H) + (int64_t)P.rank * P.H + row;
+#pragma unroll
+            for (int rk = 0; rk < DR_MAXTP; ++rk)
+              if (rk < P.tp) P.xin[rk][off] = v;
+          } else {
+            hc[row] = __ldcg(hc + row) + v;
+          }
         } else {  // DP_DOWN: this CTA's partial of the tile into its slot;
                   // the tile's last CTA zeroes the slots no CTA fills
           const long long S = (long long)d.T * d.C;
           const int c0 = dr_cta_of((long long)tile * d.C, S, d.C);
           const int c1 = dr_cta_of((long long)(tile + 1) * d.C - 1, S, d.C);
-          P.pres[(int64_t)(c - c0) * P.H + row] = v;
-          if (c == c1)
-            for (int sl = c1 - c0 + 1; sl < P.nsf; ++sl) P.pres[(int64_t)sl * P.H + row] = 0.f;
+          if (tp) {
+            const int64_t base = dr_xin_region(L & 1, 1, P.tp, P.H) + (int64_t)P.rank * P.nsf * P.H + row;
+#pragma unroll
+            for (int rk = 0; rk < DR_MAXTP; ++rk) {
+              if (rk >= P.tp) break;
+              float* dst = P.xin[rk] + base;
+              dst[(int64_t)(c - c0) * P.H] = v;
+              if (c == c1)
+                for (int sl = c1 - c0 + 1; sl < P.nsf; ++sl) dst[(int64_t)sl * P.H] = 0.f;
+            }
+          } else {
+            P.pres[(int64_t)(c - c0) * P.H + row] = v;
+            if (c == c1)
+              for (int sl = c1 - c0 + 1; sl < P.nsf; ++sl) P.pres[(int64_t)sl * P.H + row] = 0.f;
+          }
         }
       }
+      if (tp && (kind == DP_O || kind == DP_DOWN)) dr_xarrive(P, kind == DP_O ? 0 : 1);
     }
     dr_grid_arrive(P);
     dr_mark(P, ph, 3);
@@ -1031,8 +1188,19 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P)
 }
 
 // ------------------------------------------------------------------ ring layout
+// 16 bytes of a packed row.  Rows are 16-byte aligned only when K is a
+// multiple of 512 (K * 33/32 bytes per row); for other K (multiples of 64)
+// every row, scale and code offset is even, so the bytes are read as u16.
+__device__ __forceinline__ uint4 dr_ld16_row(const uint8_t* p) {
+  if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) return *reinterpret_cast<const uint4*>(p);
+  const uint16_t* h = reinterpret_cast<const uint16_t*>(p);
+  return make_uint4(h[0] | (uint32_t)h[1] << 16, h[2] | (uint32_t)h[3] << 16, h[4] | (uint32_t)h[5] << 16,
+                    h[6] | (uint32_t)h[7] << 16);
+}
+
 // One thread per 16-byte chunk of the output: block (t, c) = 16 rows x 512
-// codes in swizzled boxes, then the rows' 8 group scales of chunk c.
+// codes in swizzled boxes, then the rows' 8 group scales of chunk c.  Codes
+// and scales past K (a last chunk of fewer than 512 codes) are zero.
 __global__ void k_ring_pack(const uint8_t* __restrict__ W, int64_t nchunk16, int K, int C, int f2,
                             uint8_t* __restrict__ dst) {
   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -1054,19 +1222,39 @@ __global__ void k_ring_pack(const uint8_t* __restrict__ W, int64_t nchunk16, int
     srcoff = (int64_t)c * 16;
   }
   const int64_t row = f2 ? (r < 8 ? t * 8 + r : (int64_t)f2 + t * 8 + (r - 8)) : t * 16 + r;
-  *reinterpret_cast<uint4*>(dst + e * 16) = *reinterpret_cast<const uint4*>(W + row * rb + srcoff);
+  const uint8_t* src = W + row * rb + srcoff;
+  uint4 v = make_uint4(0, 0, 0, 0);
+  if (q < 512) {
+    if (srcoff - K / 32 < K) v = dr_ld16_row(src);  // K is a multiple of 64
+  } else {
+    const int ng = K / 64, g0 = c * 8;
+    if (g0 + 8 <= ng) {
+      v = dr_ld16_row(src);
+    } else if (g0 < ng) {  // scales of the groups that exist; zero scales after them
+      uint16_t h[8];
+      for (int i = 0; i < 8; ++i) h[i] = g0 + i < ng ? reinterpret_cast<const uint16_t*>(src)[i] : 0;
+      v = make_uint4(h[0] | (uint32_t)h[1] << 16, h[2] | (uint32_t)h[3] << 16, h[4] | (uint32_t)h[5] << 16,
+                     h[6] | (uint32_t)h[7] << 16);
+    }
+  }
+  *reinterpret_cast<uint4*>(dst + e * 16) = v;
 }
 
 int dr_repack(const uint8_t* W, int64_t rows, int K, int f2, uint8_t* dst, cudaStream_t st) {
-  Q8_CHECK_ARG(K % DR_CK == 0 && rows % 16 == 0 && (f2 == 0 || 2 * (int64_t)f2 == rows),
+  Q8_CHECK_ARG(K % 64 == 0 && rows % 16 == 0 && (f2 == 0 || 2 * (int64_t)f2 == rows),
                "ring layout: unsupported matrix %lld x %d", (long long)rows, K);
-  const int C = K / DR_CK;
+  const int C = dr_kpad(K) / DR_CK;
   const int64_t n = rows / 16 * C * (DR_BLOCK / 16);
   k_ring_pack<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(W, n, K, C, f2, dst);
   return launch_check("k_ring_pack");
 }
 
 // ------------------------------------------------------------------ host side
+size_t dr_rx_bytes(int tp, int H) {
+  const size_t inbox = (size_t)dr_xin_region(2, 0, tp, H) * 4;
+  return ((inbox + 255) & ~(size_t)255) + 256;
+}
+
 size_t dr_apart_floats(int nkv, int nsplit, int hd) {
   return (size_t)nkv * nsplit * (DR_GMAX * hd + 2 * DR_GMAX + 4);
 }
@@ -1090,9 +1278,10 @@ bool dr_supported(int H, int nh, int nkv, int hd, int F, int V, int page, const 
   if (hd != 64 && hd != 128) return no("head_dim must be 64 or 128");
   if (nkv < 1 || nh % nkv != 0 || nh / nkv > DR_GMAX) return no("more than 4 q heads per kv head");
   const int qd = nh * hd, nqkv = qd + 2 * nkv * hd;
-  if (H % DR_CK || qd % DR_CK || F % DR_CK) return no("hidden, q width and FFN width must be multiples of 512");
+  if (H % DR_CK) return no("hidden must be a multiple of 512");
+  if (qd % 64 || F % 64) return no("q width and FFN width must be multiples of 64");
   if (nqkv % 16 || H % 16 || V % 16) return no("output widths must be multiples of 16");
-  if (std::max({H, qd, F}) > 16384 || H > 8192) return no("inputs too wide for the staging");
+  if (std::max({H, dr_kpad(qd), dr_kpad(F)}) > 16384 || H > 8192) return no("inputs too wide for the staging");
   if (page % 16) return no("KV page must be a multiple of 16 positions");
   const int G = num_sms();
   if (nkv > G) return no("more kv heads than SMs");
@@ -1102,17 +1291,23 @@ bool dr_supported(int H, int nh, int nkv, int hd, int F, int V, int page, const 
     const int tiles = split ? ((int)((long long)T * C / G) + C - 1) / C + 2 : (T + G - 1) / G + 1;
     return (size_t)K * 3 + 16 + (size_t)tiles * DR_CW * 16 * 4 <= (size_t)DR_XQ_BYTES;
   };
-  if (!fits(H, nqkv / 16, false) || !fits(qd, H / 16, false) || !fits(H, F / 8, false) || !fits(F, H / 16, true) ||
-      !fits(H, V / 16, false))
+  const int qdp = dr_kpad(qd), Fp = dr_kpad(F);
+  if (!fits(H, nqkv / 16, false) || !fits(qdp, H / 16, false) || !fits(H, F / 8, false) ||
+      !fits(Fp, H / 16, true) || !fits(H, V / 16, false))
     return no("staging area too small");
   if (H > 16 * DR_CW * 32) return no("hidden wider than the one-item-per-thread RMSNorm staging");
-  if (dr_down_nsf(H, F, G) > DR_NS) return no("down tiles would span too many CTAs");
+  if (dr_down_nsf(H, Fp, G) > DR_NS) return no("down tiles would span too many CTAs");
   return true;
 }
 
 template <int HD>
-static int dr_attr() {
-  Q8_CUDA(cudaFuncSetAttribute(k_decode_ring<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, DR_SMEM));
+static int dr_attr(int* per_sm) {
+  Q8_CUDA(cudaFuncSetAttribute(k_decode_ring<HD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, DR_SMEM));
+  Q8_CUDA(cudaFuncSetAttribute(k_decode_ring<HD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, DR_SMEM));
+  int a = 0, b = 0;
+  Q8_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&a, k_decode_ring<HD, false>, DR_THREADS, DR_SMEM));
+  Q8_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_decode_ring<HD, true>, DR_THREADS, DR_SMEM));
+  *per_sm = std::min(a, b);
   return Q8_OK;
 }
 
@@ -1122,13 +1317,8 @@ int dr_prepare(int hd, int* grid) {
   int dev = 0, coop = 0, per_sm = 0;
   Q8_CUDA(cudaGetDevice(&dev));
   Q8_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
-  if (hd == 128) {
-    Q8_TRY(dr_attr<128>());
-    Q8_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_ring<128>, DR_THREADS, DR_SMEM));
-  } else {
-    Q8_TRY(dr_attr<64>());
-    Q8_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_ring<64>, DR_THREADS, DR_SMEM));
-  }
+  if (hd == 128) Q8_TRY(dr_attr<128>(&per_sm));
+  else Q8_TRY(dr_attr<64>(&per_sm));
   *grid = (coop && per_sm >= 1) ? num_sms() : 0;
   return Q8_OK;
 }
@@ -1146,8 +1336,11 @@ int dr_launch(const DrParams& p, int grid, cudaStream_t st) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = p.hd == 128 ? cudaLaunchKernelEx(&cfg, k_decode_ring<128>, p)
-                              : cudaLaunchKernelEx(&cfg, k_decode_ring<64>, p);
+  const bool xp = p.tp > 1;
+  cudaError_t e = p.hd == 128 ? (xp ? cudaLaunchKernelEx(&cfg, k_decode_ring<128, true>, p)
+                                    : cudaLaunchKernelEx(&cfg, k_decode_ring<128, false>, p))
+                              : (xp ? cudaLaunchKernelEx(&cfg, k_decode_ring<64, true>, p)
+                                    : cudaLaunchKernelEx(&cfg, k_decode_ring<64, false>, p));
   if (e != cudaSuccess) {
     cudaGetLastError();
     set_error("launch k_decode_ring: %s", cudaGetErrorString(e));

@@ -21,6 +21,7 @@ constexpr int DR_XQ_BYTES = 48 * 1024;           // activation digits + per-warp
 constexpr int DR_NS = 3;                         // partial slots of a down tile shared by CTAs
 constexpr int DR_GMAX = 4;                       // q heads per kv head
 constexpr int DR_MAXSPLIT = 128;                 // attention context splits per kv head
+constexpr int DR_MAXTP = 8;                      // tensor-parallel ranks
 
 struct DrLayer {
   // each matrix in ring layout: block (t, c) of 16-row tile t and 512-code
@@ -75,19 +76,51 @@ struct DrParams {
   int* status;                 // device status word (zero at rest)
   unsigned long long* trace;   // optional: CTA 0's globaltimer marks [phase][4] (wait done, staged,
                                // streamed, arrived)
+  int qdp, Fp;                 // o_proj / down_proj inputs rounded up to 512 (zero-padded ring blocks)
+  // tensor parallelism (tp > 1): q|k|v, gate|up and the vocabulary rows are
+  // this rank's shard; o_proj and down_proj are row-parallel: every CTA stores
+  // its partial rows into every rank's inbox (plain stores over NVLink), fences
+  // at system scope and counts itself in every rank's arrival counter; the
+  // next phase waits for the CTAs of all ranks and adds the partials in rank
+  // order, so every rank holds the same residual
+  int tp, rank;
+  int V_off;                   // first vocabulary row of this rank (argmax keys are global rows)
+  int gsum;                    // CTAs of all ranks (arrivals per exchange)
+  float* xin[DR_MAXTP];        // every rank's inbox, mapped here: [parity][o | down][tp][slots][H]
+  unsigned long long* xcnt[DR_MAXTP];   // every rank's monotonic arrival counters [o, down, lm_head]
+  unsigned long long* xamax[DR_MAXTP];  // every rank's argmax keys [step parity]
+  unsigned long long* xstep;   // this rank's completed steps
+  float* xin_me;               // xin[rank]
+  unsigned long long* xcnt_me; // xcnt[rank]
+  unsigned long long* xamax_me;// xamax[rank]
+  float* hm;                   // residual after o_proj [H]
 };
+
+// Inbox of the row-parallel exchange: floats from region (parity, kind) on
+// (kind 0: o_proj, one slot per rank; kind 1: down_proj, nsf slots per rank).
+__host__ __device__ inline int64_t dr_xin_region(int par, int kind, int tp, int H) {
+  return (int64_t)(par * 2 + kind) * tp * DR_NS * H;
+}
+// Bytes of one rank's exchange block: the inbox, then 256 bytes of counters
+// (xcnt [4] at +0, xamax [2] at +64, xstep at +128).
+size_t dr_rx_bytes(int tp, int H);
 
 // Host side (q8_decode_ring.cu).
 // Whether the ring step supports these model dimensions on this device
 // (one sequence, one GPU); *why gets the reason when it does not.
+// Dimensions are this rank's (tensor-parallel shards).
 bool dr_supported(int H, int nh, int nkv, int hd, int F, int V, int page, const char** why);
+// K rounded up to whole 512-code ring chunks.
+inline int dr_kpad(int K) { return (K + DR_CK - 1) / DR_CK * DR_CK; }
 int dr_prepare(int hd, int* grid);  // kernel attributes, residency check; grid = CTAs (one per SM)
 size_t dr_apart_floats(int nkv, int nsplit, int hd);
 int dr_nsplit(int G, int nkv);
 int dr_down_nsf(int H, int F, int G);
 int dr_launch(const DrParams& p, int grid, cudaStream_t st);
 // Copies a packed-row matrix (rows x K, SwiGLU: 2 F rows with f2 = F) into
-// ring layout at dst (rows * (K + K/32) bytes).
+// ring layout at dst (dr_ring_bytes(rows, K) bytes; codes and scales past K
+// are zero).
 int dr_repack(const uint8_t* W, int64_t rows, int K, int f2, uint8_t* dst, cudaStream_t st);
+inline size_t dr_ring_bytes(int64_t rows, int K) { return (size_t)(rows / 16) * (dr_kpad(K) / DR_CK) * DR_BLOCK; }
 
 }  // namespace q8

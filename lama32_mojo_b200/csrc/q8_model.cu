@@ -13,6 +13,7 @@
 #include "q8_kernels.h"
 #include "safetensors.h"
 
+#include <array>
 #include <cmath>
 #include <fcntl.h>
 #include <nccl.h>
@@ -216,7 +217,10 @@ struct q8_ctx {
   int *dr_aticket = nullptr, *dr_lm_ticket = nullptr, *dr_status = nullptr, *dr_status_pin = nullptr;
   unsigned long long* dr_amax = nullptr;
   unsigned int* dr_bar = nullptr;
-  uint8_t* dr_wring = nullptr;  // the weight arena again, matrices in ring layout (q8_decode_ring.cu)
+  uint8_t* dr_wring = nullptr;  // the matrices again, in ring layout (q8_decode_ring.cu)
+  std::vector<std::array<uint8_t*, 4>> dr_rw;  // per layer: q|k|v, o, gate|up, down in dr_wring
+  uint8_t* dr_rlm = nullptr;                   // lm_head rows of this rank in dr_wring
+  float* dr_hm = nullptr;                      // residual after o_proj (tensor parallel)
   bool dr_packed = false;       // dr_wring matches the loaded weights
   unsigned long long* dr_trace = nullptr;  // CTA 0's phase marks of the last profiled ring step
   bool dr_traced = false;
@@ -305,15 +309,14 @@ static bool p2p_fits(q8_ctx* c, int T) { return c->ar.ok && (int64_t)T * c->H <=
 static int ring_prepare(q8_ctx* c) {
   if (!c->dr || c->dr_packed) return Q8_OK;
   const int H = c->H, nqkv = c->qd + 2 * c->kvd;
-  auto rp = [&](const uint8_t* w) { return c->dr_wring + (w - c->warena); };
   for (int L = 0; L < c->cfg.layers; ++L) {
     const LayerW& w = c->layers[L];
-    Q8_TRY(dr_repack(w.qkv, nqkv, H, 0, rp(w.qkv), c->st));
-    Q8_TRY(dr_repack(w.o, H, c->qd, 0, rp(w.o), c->st));
-    Q8_TRY(dr_repack(w.gu, 2 * (int64_t)c->F, H, c->F, rp(w.gu), c->st));
-    Q8_TRY(dr_repack(w.down, H, c->F, 0, rp(w.down), c->st));
+    Q8_TRY(dr_repack(w.qkv, nqkv, H, 0, c->dr_rw[L][0], c->st));
+    Q8_TRY(dr_repack(w.o, H, c->qd, 0, c->dr_rw[L][1], c->st));
+    Q8_TRY(dr_repack(w.gu, 2 * (int64_t)c->F, H, c->F, c->dr_rw[L][2], c->st));
+    Q8_TRY(dr_repack(w.down, H, c->F, 0, c->dr_rw[L][3], c->st));
   }
-  Q8_TRY(dr_repack(c->lm_head, c->V_loc, H, 0, rp(c->lm_head), c->st));
+  Q8_TRY(dr_repack(c->lm_head, c->V_loc, H, 0, c->dr_rlm, c->st));
   Q8_CUDA(cudaStreamSynchronize(c->st));
   c->dr_packed = true;
   return Q8_OK;
@@ -330,18 +333,36 @@ static bool ring_ok(q8_ctx* c, int T, bool blocks, int lrow0, int lrows) {
 static int ring_step(q8_ctx* c, bool gen) {
   DrParams p{};
   p.H = c->H; p.nh = c->nh; p.nkv = c->nkv; p.hd = c->hd; p.qd = c->qd; p.nqkv = c->qd + 2 * c->kvd;
-  p.F = c->F; p.V = c->V; p.L = c->cfg.layers; p.eps = c->cfg.eps;
-  p.layers = c->dr_layers; p.embed = c->embed; p.lm_head = c->dr_wring + (c->lm_head - c->warena);
+  p.F = c->F; p.V = c->V_loc; p.L = c->cfg.layers; p.eps = c->cfg.eps;
+  p.layers = c->dr_layers; p.embed = c->embed; p.lm_head = c->dr_rlm;
   p.final_norm = c->final_norm;
   p.ids = c->ids_d; p.pos = c->pos_d; p.seq = c->seq_d; p.inv_freq = c->inv_freq_d;
   p.page = c->page; p.bt = c->bt_d; p.max_pages = c->max_pages;
-  p.h0 = c->h; p.h1 = c->dr_h1; p.pres = c->dr_pres; p.nsf = dr_down_nsf(c->H, c->F, c->dr_grid); p.qkv = c->qkv; p.ao = c->ao32; p.act = c->act32;
+  p.qdp = dr_kpad(c->qd); p.Fp = dr_kpad(c->F);
+  p.h0 = c->h; p.h1 = c->dr_h1; p.pres = c->dr_pres; p.nsf = dr_down_nsf(c->H, p.Fp, c->dr_grid);
+  p.qkv = c->qkv; p.ao = c->ao32; p.act = c->act32;
   p.logits = c->logits; p.apart = c->dr_apart; p.aticket = c->dr_aticket; p.nsplit = c->dr_nsplit;
   p.amax = c->dr_amax; p.lm_ticket = c->dr_lm_ticket; p.argmax = c->argmax_d;
   p.gen = gen ? 1 : 0; p.hist = c->hist_d; p.ctr = c->ctr_d; p.hist_cap = c->hist_cap;
   p.bar = c->dr_bar; p.status = c->dr_status;
   p.trace = c->profiling ? c->dr_trace : nullptr;
   c->dr_traced = c->profiling;
+  p.tp = c->tp_size; p.rank = c->tp_rank; p.V_off = c->V_off; p.gsum = c->tp_size * c->dr_grid;
+  if (c->tp_size > 1) {
+    const size_t xo = (size_t)dr_xin_region(2, 0, c->tp_size, c->H) * 4;
+    const size_t co = (xo + 255) & ~(size_t)255;  // counters after the inbox (dr_rx_bytes)
+    for (int k = 0; k < c->tp_size; ++k) {
+      uint8_t* b = c->ar.peers.rx[k];
+      p.xin[k] = reinterpret_cast<float*>(b);
+      p.xcnt[k] = reinterpret_cast<unsigned long long*>(b + co);
+      p.xamax[k] = reinterpret_cast<unsigned long long*>(b + co + 64);
+    }
+    p.xstep = reinterpret_cast<unsigned long long*>(c->ar.rx + co + 128);
+    p.xin_me = p.xin[c->tp_rank];
+    p.xcnt_me = p.xcnt[c->tp_rank];
+    p.xamax_me = p.xamax[c->tp_rank];
+    p.hm = c->dr_hm;
+  }
   return dr_launch(p, c->dr_grid, c->st);
 }
 
@@ -677,6 +698,10 @@ static int status_check(q8_ctx* c) {
   Q8_CUDA(cudaMemsetAsync(c->dr_lm_ticket, 0, 4, c->st));
   Q8_CUDA(cudaMemsetAsync(c->dr_amax, 0, 8, c->st));
   Q8_CUDA(cudaStreamSynchronize(c->st));
+  if (v == Q8_ERR_COMM) {
+    set_error("decode step: a tensor-parallel exchange wait timed out (a peer rank did not arrive)");
+    return Q8_ERR_COMM;
+  }
   set_error("decode step: a bounded device wait timed out (device status %d)", v);
   return Q8_ERR_TIMEOUT;
 }
@@ -799,7 +824,7 @@ static int destroy_impl(q8_ctx* c) {
                   c->logits, c->part, c->xs_in, c->xs_ao, c->xs_act, c->xn32, c->ao32, c->act32, c->am_val, c->am_gval, c->lg_gather,
                   c->am_idx, c->am_gidx, c->dr_layers, c->dr_h1, c->dr_pres, c->dr_apart, c->dr_aticket,
                   c->dr_lm_ticket, c->dr_status, c->dr_amax, c->dr_bar, c->dr_trace, c->dr_wring,
-                  c->samp_ws, c->samp_u, c->samp_logits};
+                  c->dr_hm, c->samp_ws, c->samp_u, c->samp_logits};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   if (c->pin) cudaFreeHost(c->pin);
@@ -1032,14 +1057,43 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
   if ((s = gemv_d_prepare(std::max({ceil_div(c->qd + 2 * c->kvd, 16), ceil_div(H, 16), ceil_div(c->F, 8),
                                     ceil_div(c->V_loc, 16)})))) return bail(s);
 
-  // ---- weight-ring decode step for one-sequence greedy decode on one GPU
+  if (tp_size > 1) {
+    ncclUniqueId id;
+    memcpy(&id, nccl_id, 128);
+    ncclResult_t r = ncclCommInitRank(&c->comm, tp_size, id, tp_rank);
+    if (r != ncclSuccess) return bail((set_error("ncclCommInitRank: %s", ncclGetErrorString(r)), Q8_ERR_COMM));
+    // decode-sized row-parallel sums over P2P, and the one-launch step's
+    // exchange block (every rank takes this step)
+    if ((s = ar_setup(&c->ar, c->comm, tp_size, tp_rank, (int64_t)std::max(1, max_seqs) * H,
+                      dr_rx_bytes(tp_size, H), c->st)))
+      return bail(s);
+    if (c->ar.ok) {
+      if (cudaMallocHost((void**)&c->ar_status_pin, 4) != cudaSuccess)
+        return bail((set_error("pinned status allocation failed"), Q8_ERR_OOM));
+      *c->ar_status_pin = 0;
+    }
+  }
+
+  // ---- weight-ring decode step for one-sequence greedy decode
   // (default; Q8_RING=0 keeps those steps on the per-operation kernels)
   {
     const char* e = getenv("Q8_RING");
     const char* why = nullptr;
-    if (!(e && e[0] == '0') && tp_size == 1 && !c->bf16 &&
-        dr_supported(H, c->nh, c->nkv, c->hd, c->F, c->V, c->page, &why)) {
+    if (!(e && e[0] == '0') && (tp_size == 1 || c->ar.ok) && !c->bf16 &&
+        dr_supported(H, c->nh, c->nkv, c->hd, c->F, c->V_loc, c->page, &why)) {
       if ((s = dr_prepare(c->hd, &c->dr_grid))) return bail(s);
+    }
+    if (tp_size > 1) {  // every rank runs the ring step, with the same grid, or none does
+      int* d = nullptr;
+      if ((s = dmalloc((void**)&d, 8))) return bail(s);
+      int v[2] = {c->dr_grid, -c->dr_grid}, o[2] = {0, 0};
+      bool ok = cudaMemcpyAsync(d, v, 8, cudaMemcpyHostToDevice, c->st) == cudaSuccess &&
+                ncclAllReduce(d, d, 2, ncclInt32, ncclMin, c->comm, c->st) == ncclSuccess &&
+                cudaMemcpyAsync(o, d, 8, cudaMemcpyDeviceToHost, c->st) == cudaSuccess &&
+                cudaStreamSynchronize(c->st) == cudaSuccess;
+      cudaFree(d);
+      if (!ok) return bail((set_error("decode step: rank agreement failed"), Q8_ERR_COMM));
+      if (o[0] != -o[1]) c->dr_grid = 0;  // some rank cannot (or has another grid)
     }
     if (c->dr_grid > 0) {
       const int nqkv = c->qd + 2 * c->kvd;
@@ -1060,37 +1114,42 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
       if (cudaMallocHost((void**)&c->dr_status_pin, 4) != cudaSuccess)
         return bail((set_error("cudaMallocHost failed"), Q8_ERR_OOM));
       *c->dr_status_pin = 0;
-      if ((s = dmalloc((void**)&c->dr_wring, c->wbytes))) return bail(s);
-      auto rp = [&](const uint8_t* w) { return (const uint8_t*)(c->dr_wring + (w - c->warena)); };
+      // ring-layout copies: o_proj and down_proj inputs padded to whole
+      // 512-code chunks (tensor-parallel K slices need not be)
+      size_t rofs = 0;
+      std::vector<std::array<size_t, 4>> ro(C.layers);
+      auto rtake = [&](size_t b) {
+        const size_t o = rofs;
+        rofs += (b + 255) & ~(size_t)255;
+        return o;
+      };
+      for (int L = 0; L < C.layers; ++L)
+        ro[L] = {rtake(dr_ring_bytes(nqkv, H)), rtake(dr_ring_bytes(H, c->qd)), rtake(dr_ring_bytes(2 * c->F, H)),
+                 rtake(dr_ring_bytes(H, c->F))};
+      const size_t rlm = rtake(dr_ring_bytes(c->V_loc, H));
+      if ((s = dmalloc((void**)&c->dr_wring, rofs))) return bail(s);
+      if (tp_size > 1 && (s = dmalloc((void**)&c->dr_hm, (size_t)H * 4))) return bail(s);
+      c->dr_rlm = c->dr_wring + rlm;
+      c->dr_rw.resize(C.layers);
       std::vector<DrLayer> dl(C.layers);
       for (int L = 0; L < C.layers; ++L) {
         const LayerW& w = c->layers[L];
-        dl[L] = DrLayer{rp(w.qkv), rp(w.o), rp(w.gu), rp(w.down), w.in_norm, w.post_norm, w.q_norm, w.k_norm,
-                        c->kpool + (size_t)L * c->layer_kv, c->vpool + (size_t)L * c->layer_kv};
+        for (int j = 0; j < 4; ++j) c->dr_rw[L][j] = c->dr_wring + ro[L][j];
+        dl[L] = DrLayer{c->dr_rw[L][0], c->dr_rw[L][1], c->dr_rw[L][2], c->dr_rw[L][3], w.in_norm, w.post_norm,
+                        w.q_norm, w.k_norm, c->kpool + (size_t)L * c->layer_kv, c->vpool + (size_t)L * c->layer_kv};
       }
       if (cudaMemcpy(c->dr_layers, dl.data(), sizeof(DrLayer) * C.layers, cudaMemcpyHostToDevice) != cudaSuccess)
         return bail((set_error("decode step layer table upload failed"), Q8_ERR_CUDA));
       if ((s = dmalloc((void**)&c->dr_trace, sizeof(unsigned long long) * 4 * (5 * C.layers + 1)))) return bail(s);
+      // algorithmic bytes: the packed rows of this rank's matrices (the
+      // zero padding of the ring layout is not counted)
       c->dr_wbytes = (double)C.layers * ((double)nqkv * q8_row_bytes(H) + (double)H * q8_row_bytes(c->qd) +
                                          2.0 * c->F * q8_row_bytes(H) + (double)H * q8_row_bytes(c->F)) +
-                     (double)c->V * q8_row_bytes(H);
+                     (double)c->V_loc * q8_row_bytes(H);
       c->dr = true;
     }
   }
 
-  if (tp_size > 1) {
-    ncclUniqueId id;
-    memcpy(&id, nccl_id, 128);
-    ncclResult_t r = ncclCommInitRank(&c->comm, tp_size, id, tp_rank);
-    if (r != ncclSuccess) return bail((set_error("ncclCommInitRank: %s", ncclGetErrorString(r)), Q8_ERR_COMM));
-    // decode-sized row-parallel sums over P2P (every rank takes this step)
-    if ((s = ar_setup(&c->ar, c->comm, tp_size, tp_rank, (int64_t)std::max(1, max_seqs) * H, c->st))) return bail(s);
-    if (c->ar.ok) {
-      if (cudaMallocHost((void**)&c->ar_status_pin, 4) != cudaSuccess)
-        return bail((set_error("pinned status allocation failed"), Q8_ERR_OOM));
-      *c->ar_status_pin = 0;
-    }
-  }
   *out = c;
   return Q8_OK;
 }

@@ -195,6 +195,9 @@ PRESETS: Dict[str, Config] = {
                           "llama3", 32.0, 1.0, 4.0, 8192.0, False, True),
     "small-qwen3": Config("small-qwen3", 1024, 2, 8, 2, 128, 1536, 3072, 1e-6, 1000000.0,
                           "default", 1.0, 1.0, 4.0, 8192.0, True, False),
+    # q width (384) and FFN width (768) that the ring layout pads to 512 / 1024
+    "small-pad": Config("small-pad", 512, 2, 6, 2, 64, 768, 1024, 1e-5, 500000.0,
+                        "llama3", 32.0, 1.0, 4.0, 8192.0, False, True),
     # heads, FFN rows and vocabulary that split over 8 tensor-parallel ranks
     "tiny-tp8": Config("tiny-tp8", 512, 2, 8, 8, 64, 1024, 2048, 1e-5, 500000.0,
                        "llama3", 32.0, 1.0, 4.0, 8192.0, False, False),

@@ -298,7 +298,7 @@ def test_prefill_attention_context_splits(cuda, cfgname):
     m.close()
 
 
-@pytest.mark.parametrize("cfgname", ["small-llama", "small-qwen3", "tiny-llama-untied"])
+@pytest.mark.parametrize("cfgname", ["small-llama", "small-qwen3", "tiny-llama-untied", "small-pad"])
 def test_ring_decode_step_matches_per_op(cuda, cfgname, monkeypatch):
     """The one-launch weight-ring decode step (default for one-sequence greedy
     decode) against the per-operation kernels (Q8_RING=0) on the same

@@ -43,8 +43,11 @@ def _rank(rank, world, port, cfgname, ids, steps, q, weights="q8"):
         out = {"hidden1": m.forward_hidden(ids, 1)}
         out["logits"] = m.forward(ids)
         toks = [int(np.argmax(out["logits"]))]
+        m.set_profiling(True)
         for _ in range(steps):
             toks.append(m.forward_argmax([toks[-1]]))
+        out["ring"] = "decode_step" in m.profile()  # the one-launch step with its in-kernel exchange
+        m.set_profiling(False)
         out["tokens"] = toks
         m.forward(ids[:3], seq=1)
         out["gen"] = m.generate([toks[0]], [1], 3)[:, 0].tolist()
@@ -89,6 +92,8 @@ def test_tp2_matches_oracle(cuda, cfgname, weights):
     ocfg = O.PRESETS[cfgname].replace(weights=weights)
     ids = O.random_ids(ocfg, 9, seed=41)
     out = _run_tp2(cfgname, ids, weights)
+    # widths and vocabulary shards of tiny-llama-untied suit the one-launch step
+    assert out["ring"] == (cfgname == "tiny-llama-untied" and weights == "q8")
     ck = O.make_q8_checkpoint(ocfg) if weights == "q8" else O.make_bf16_checkpoint(ocfg)
     orc = O.OracleModel(ocfg, ck)
     ref = orc.forward(ids)
