@@ -661,7 +661,7 @@ __device__ __forceinline__ unsigned long long dr_key(float v, int idx) {
 template <int HD>
 __device__ void dr_attn(const DrParams& P, int L, uint8_t* ring, uint64_t* full, uint64_t* empty, int& u, float* sQ,
                         float* sP, float* sKn, float* sVn, float* sX, float (*sm_m)[DR_GMAX],
-                        float (*sm_l)[DR_GMAX], int* s_last) {
+                        float (*sm_l)[DR_GMAX], int* s_last, const float* sRope) {
   constexpr int E = HD / 32, CH = HD / 4, J = HD / 32;
   const int c = blockIdx.x, ns = P.nsplit;
   if (c >= P.nkv * ns) return;
@@ -701,11 +701,11 @@ __device__ void dr_attn(const DrParams& P, int L, uint8_t* ring, uint64_t* full,
 #pragma unroll
         for (int j = 0; j < J; ++j) v[j] = bf16_bits_to_f32(nw[lane + 32 * j]) * v[j] * inv;
       }
-      const float fp = (float)p;
 #pragma unroll
       for (int j = 0; j < J / 2; ++j) {
         float sn, cs;
-        sincosf(fp * P.inv_freq[lane + 32 * j], &sn, &cs);
+        cs = sRope[lane + 32 * j];  // cos / sin of the step's position, made at launch
+        sn = sRope[64 + lane + 32 * j];
         const float x0 = v[j], x1 = v[j + J / 2];
         v[j] = x0 * cs - x1 * sn;
         v[j + J / 2] = x1 * cs + x0 * sn;
@@ -787,6 +787,10 @@ __device__ void dr_attn(const DrParams& P, int L, uint8_t* ring, uint64_t* full,
         s[g] = (lane & 1) ? other + part : part + other;
       }
     }
+    // the K rows are read: the producer may refill that slot during the PV
+    // product (the next block's K then loads while this block's V is used)
+    __syncwarp();
+    if (lane == 0) dr_arrive(&empty[sk]);
 #pragma unroll
     for (int g = 0; g < DR_GMAX; ++g) {
       if (g >= G) break;
@@ -830,10 +834,7 @@ __device__ void dr_attn(const DrParams& P, int L, uint8_t* ring, uint64_t* full,
       }
     }
     __syncwarp();
-    if (lane == 0) {
-      dr_arrive(&empty[sk]);
-      dr_arrive(&empty[sv]);
-    }
+    if (lane == 0) dr_arrive(&empty[sv]);
     u += 2;
   }
 #pragma unroll
@@ -980,6 +981,7 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P)
   __shared__ int s_last;
   __shared__ unsigned long long s_key[DR_CW];
   __shared__ unsigned long long s_epoch;  // completed steps of this rank (tensor parallel)
+  __shared__ float s_rope[128];           // cos | sin of the step's position x inv_freq (RoPE)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == DR_CW * 32) {
@@ -1003,8 +1005,14 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P)
   // peer's launch begins)
   if constexpr (XP) {
     if (threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile unsigned long long*>(P.xstep);
-    dr_csync();
   }
+  if (threadIdx.x < HD / 2) {  // the same position for every layer of the step
+    float sn, cs;
+    sincosf((float)P.pos[0] * P.inv_freq[threadIdx.x], &sn, &cs);
+    s_rope[threadIdx.x] = cs;
+    s_rope[64 + threadIdx.x] = sn;
+  }
+  dr_csync();
   int u = 0;
   unsigned int target = 0;
   const int nphase = 5 * P.L + 1;
@@ -1014,7 +1022,8 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P)
     if (kind == DP_ATTN) {
       dr_grid_wait(P, target);
       dr_mark(P, ph, 0);
-      dr_attn<HD>(P, L, ring, full, empty, u, sQ, sP, sKn, sVn, reinterpret_cast<float*>(xq), sm_m, sm_l, &s_last);
+      dr_attn<HD>(P, L, ring, full, empty, u, sQ, sP, sKn, sVn, reinterpret_cast<float*>(xq), sm_m, sm_l, &s_last,
+                  s_rope);
       dr_mark(P, ph, 1);
       dr_mark(P, ph, 2);
       dr_grid_arrive(P);
