@@ -407,14 +407,13 @@ __device__ __forceinline__ void dr_digits16(const float (&v)[16], bool valid, in
   if (sq == 0) fcol[gi] = make_float4(e, e / 254.0f, e / 64516.0f, 0.f);
 }
 
-enum { DS_F32 = 0, DS_EMBED = 1, DS_FOLD = 2 };
-
-// 16 values x[k0 .. k0+15] of the phase's input vector; every load of the
-// item is in flight before the first is used.
-template <int KIND, bool XP>
-__device__ __forceinline__ void dr_load16(const DrParams& P, const float* src, const float* slots, int nslots, int k0,
-                                          float (&v)[16]) {
-  if constexpr (KIND == DS_EMBED) {
+// 16 values x[k0 .. k0+15] of the phase's input vector: the step's Q8
+// embedding row (embed), or src + nslots partial slots (stride H); every load
+// of the item is in flight before the first is used.
+template <bool XP>
+__device__ __forceinline__ void dr_load16(const DrParams& P, bool embed, const float* src, const float* slots,
+                                          int nslots, int k0, float (&v)[16]) {
+  if (embed) {
     const int64_t rb = (int64_t)P.H + P.H / 32;
     const uint8_t* row = P.embed + (int64_t)P.ids[0] * rb;
     const float s = __half2float(__ushort_as_half(reinterpret_cast<const unsigned short*>(row)[k0 / 64]));
@@ -428,7 +427,7 @@ __device__ __forceinline__ void dr_load16(const DrParams& P, const float* src, c
   float4 a[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) a[i] = __ldcg(reinterpret_cast<const float4*>(src + k0) + i);
-  if constexpr (KIND == DS_FOLD && !XP) {  // + this GPU's partial slots (<= DR_NS, stride H), in slot order
+  if constexpr (!XP) {  // + this GPU's partial slots (<= DR_NS), in slot order
     float4 pp[DR_NS][4];
 #pragma unroll
     for (int sl = 0; sl < DR_NS; ++sl)
@@ -446,7 +445,7 @@ __device__ __forceinline__ void dr_load16(const DrParams& P, const float* src, c
       }
     }
   }
-  if constexpr (KIND == DS_FOLD && XP) {  // + every rank's partial slots (stride H), in rank and slot order
+  if constexpr (XP) {  // + every rank's partial slots, in rank and slot order
     for (int s0 = 0; s0 < nslots; s0 += DR_NS) {
       float4 pp[DR_NS][4];
 #pragma unroll
@@ -474,87 +473,97 @@ __device__ __forceinline__ void dr_load16(const DrParams& P, const float* src, c
   }
 }
 
-// Stages the K inputs of a GEMV phase as digits (zero digits up to Kd): waits
-// for the previous phase of the grid (target arrivals; 0: none) or, with xc,
-// for `xtarget` arrivals of all ranks on that exchange counter; then x from
-// `kind` (DS_FOLD: src + nslots partial slots); with nw (K <= 16 x 256),
-// x = nw * x / sqrt(mean(x^2) + eps), the norm weights read before the wait;
-// with wb, this CTA's slice of the raw x is written back (the residual).
-template <int KIND, bool RMS, bool XP>
-__device__ void dr_stage(const DrParams& P, int ph, unsigned int target, const unsigned long long* xc,
-                         unsigned long long xtarget, int Kd, int K, const float* src, const float* slots, int nslots,
-                         const uint16_t* nw, float* wb, uint8_t* xq, float4* fcol, float* scr) {
-  constexpr int NT = DR_CW * 32;
+// Stages the H inputs of an RMSNorm'd GEMV phase (q|k|v, gate|up, lm_head) as
+// digits: the norm weights read first, then the wait for the previous phase
+// of the grid (target arrivals; 0: none) or, with xc, for `xtarget` arrivals
+// of all ranks on that exchange counter; then x (dr_load16), x = nw * x /
+// sqrt(mean(x^2) + eps) (one 16-value item per thread); with wb, this CTA's
+// slice of the raw x is written back (the residual).  One inlined copy of
+// this code serves every such phase (the instruction cache holds little of
+// the step).
+template <bool XP>
+__device__ __forceinline__ void dr_stage_rms(const DrParams& P, int ph, unsigned int target, const unsigned long long* xc,
+                                          unsigned long long xtarget, bool embed, const float* src, const float* slots,
+                                          int nslots, const uint16_t* nw, float* wb, uint8_t* xq, float4* fcol,
+                                          float* scr) {
+  const int K = P.H;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, sq = lane & 3;
   const int nitem = K / 16;  // quarter-groups
-  if constexpr (RMS) {
-    const bool valid = tid < nitem;
-    const int k0 = tid * 16;
-    uint4 w0 = make_uint4(0, 0, 0, 0), w1 = w0;
-    if (valid) {
-      w0 = __ldg(reinterpret_cast<const uint4*>(nw + k0));
-      w1 = __ldg(reinterpret_cast<const uint4*>(nw + k0 + 8));
+  const bool valid = tid < nitem;
+  const int k0 = tid * 16;
+  uint4 w0 = make_uint4(0, 0, 0, 0), w1 = w0;
+  if (valid) {
+    w0 = __ldg(reinterpret_cast<const uint4*>(nw + k0));
+    w1 = __ldg(reinterpret_cast<const uint4*>(nw + k0 + 8));
+  }
+  if (xc) dr_xwait(P, xc, xtarget);
+  else if (target) dr_grid_wait(P, target);
+  dr_mark(P, ph, 0);
+  float v[16];
+  float ss = 0.f;
+  if (valid) {
+    dr_load16<XP>(P, embed, src, slots, nslots, k0, v);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) ss = fmaf(v[i], v[i], ss);
+    if (wb) {
+      const int G = gridDim.x, c = blockIdx.x;
+      const int s0 = (int)((long long)K * c / G), s1 = (int)((long long)K * (c + 1) / G);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (k0 + i >= s0 && k0 + i < s1) wb[k0 + i] = v[i];
     }
-    if (xc) dr_xwait(P, xc, xtarget);
-    else if (target) dr_grid_wait(P, target);
-    dr_mark(P, ph, 0);
-    float v[16];
-    float ss = 0.f;
-    if (valid) {
-      dr_load16<KIND, XP>(P, src, slots, nslots, k0, v);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) ss = fmaf(v[i], v[i], ss);
-      if (wb) {
-        const int G = gridDim.x, c = blockIdx.x;
-        const int s0 = (int)((long long)K * c / G), s1 = (int)((long long)K * (c + 1) / G);
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          if (k0 + i >= s0 && k0 + i < s1) wb[k0 + i] = v[i];
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] = 0.f;
-    }
-    ss = warp_sum(ss);
-    if (lane == 0) scr[warp] = ss;
-    dr_csync();
-    float tot = 0.f;
-#pragma unroll
-    for (int w = 0; w < DR_CW; ++w) tot += scr[w];
-    const float inv = 1.0f / sqrtf(tot / (float)K + P.eps);
-    if (valid) {
-      const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        v[2 * i] = __uint_as_float(ww[i] << 16) * v[2 * i] * inv;
-        v[2 * i + 1] = __uint_as_float(ww[i] & 0xFFFF0000u) * v[2 * i + 1] * inv;
-      }
-    }
-    dr_digits16(v, valid, valid ? tid >> 2 : 0, sq, xq, fcol);
   } else {
-    if (xc) dr_xwait(P, xc, xtarget);
-    else if (target) dr_grid_wait(P, target);
-    dr_mark(P, ph, 0);
-    constexpr int R = 2;  // rounds whose loads are in flight together
-    const int nitem_d = Kd / 16;  // with the zero padding
-    for (int base = 0; base < nitem_d; base += R * NT) {
-      float v[R][16];
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const int item = base + r * NT + tid;
-        if (item < nitem) dr_load16<KIND, XP>(P, src, slots, nslots, item * 16, v[r]);
-      }
+    for (int i = 0; i < 16; ++i) v[i] = 0.f;
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) scr[warp] = ss;
+  dr_csync();
+  float tot = 0.f;
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const int item = base + r * NT + tid;
-        if (base + r * NT < nitem_d) {
-          const bool valid = item < nitem_d;
-          if (!valid || item >= nitem) {
+  for (int w = 0; w < DR_CW; ++w) tot += scr[w];
+  const float inv = 1.0f / sqrtf(tot / (float)K + P.eps);
+  if (valid) {
+    const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-            for (int i = 0; i < 16; ++i) v[r][i] = 0.f;
-          }
-          dr_digits16(v[r], valid, valid ? item >> 2 : 0, sq, xq, fcol);
+    for (int i = 0; i < 8; ++i) {
+      v[2 * i] = __uint_as_float(ww[i] << 16) * v[2 * i] * inv;
+      v[2 * i + 1] = __uint_as_float(ww[i] & 0xFFFF0000u) * v[2 * i + 1] * inv;
+    }
+  }
+  dr_digits16(v, valid, valid ? tid >> 2 : 0, sq, xq, fcol);
+  dr_csync();
+}
+
+// Stages the K inputs of o_proj / down_proj (plain f32 rows, zero digits up
+// to the padded Kd) after the previous phase of the grid.
+template <bool XP>
+__device__ __forceinline__ void dr_stage_plain(const DrParams& P, int ph, unsigned int target, int Kd, int K,
+                                            const float* src, uint8_t* xq, float4* fcol) {
+  constexpr int NT = DR_CW * 32;
+  const int tid = threadIdx.x, lane = tid & 31, sq = lane & 3;
+  const int nitem = K / 16;
+  dr_grid_wait(P, target);
+  dr_mark(P, ph, 0);
+  constexpr int R = 2;  // rounds whose loads are in flight together
+  const int nitem_d = Kd / 16;  // with the zero padding
+  for (int base = 0; base < nitem_d; base += R * NT) {
+    float v[R][16];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int item = base + r * NT + tid;
+      if (item < nitem) dr_load16<XP>(P, false, src, nullptr, 0, item * 16, v[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int item = base + r * NT + tid;
+      if (base + r * NT < nitem_d) {
+        const bool valid = item < nitem_d;
+        if (!valid || item >= nitem) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[r][i] = 0.f;
         }
+        dr_digits16(v[r], valid, valid ? item >> 2 : 0, sq, xq, fcol);
       }
     }
   }
@@ -1036,56 +1045,54 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P)
     float* hp = (L & 1) ? P.h0 : P.h1;  // the previous layer's
     // the stagings wait for the previous phase (after their static loads);
     // mark 0 is then the end of the wait.  Folds: the residual + the previous
-    // down_proj's partials (this GPU's slots, or every rank's, in rank order)
-    const int Lp = (kind == DP_LM ? P.L : L) - 1;
-    const float* dslots = tp ? P.xin_me + dr_xin_region(Lp & 1, 1, P.tp, P.H) : P.pres;
-    const int dn = tp ? P.tp * P.nsf : P.nsf;
-    const unsigned long long* dxc = tp ? P.xcnt_me + 1 : nullptr;
-    const unsigned long long dxt = (s_epoch * (unsigned long long)P.L + (unsigned long long)Lp + 1) *
-                                   (unsigned long long)P.gsum;
-    switch (kind) {
-      case DP_QKV:
-        if (L == 0)
-          dr_stage<DS_EMBED, true, XP>(P, ph, target, nullptr, 0, P.H, P.H, hp, nullptr, 0, ly->in_norm, hc, xq, fcol,
-                                   scr);
-        else
-          dr_stage<DS_FOLD, true, XP>(P, ph, target, dxc, dxt, P.H, P.H, tp ? P.hm : hp, dslots, dn, ly->in_norm, hc, xq,
-                                  fcol, scr);
-        break;
-      case DP_O:
-        dr_stage<DS_F32, false, XP>(P, ph, target, nullptr, 0, P.qdp, P.qd, P.ao, nullptr, 0, nullptr, nullptr, xq, fcol,
-                                scr);
-        break;
-      case DP_GU:
-        if constexpr (XP)  // + every rank's o_proj partial; the sum is kept as the mid residual
-          dr_stage<DS_FOLD, true, XP>(P, ph, target, P.xcnt_me + 0,
-                                      (s_epoch * (unsigned long long)P.L + (unsigned long long)L + 1) *
-                                          (unsigned long long)P.gsum,
-                                      P.H, P.H, hc, P.xin_me + dr_xin_region(L & 1, 0, P.tp, P.H), P.tp,
-                                      ly->post_norm, P.hm, xq, fcol, scr);
-        else
-          dr_stage<DS_F32, true, XP>(P, ph, target, nullptr, 0, P.H, P.H, hc, nullptr, 0, ly->post_norm, nullptr, xq,
-                                     fcol, scr);
-        break;
-      case DP_DOWN:
-        dr_stage<DS_F32, false, XP>(P, ph, target, nullptr, 0, P.Fp, P.F, P.act, nullptr, 0, nullptr, nullptr, xq, fcol,
-                                scr);
-        break;
-      default:
-        dr_stage<DS_FOLD, true, XP>(P, ph, target, dxc, dxt, P.H, P.H, tp ? P.hm : ((Lp & 1) ? P.h1 : P.h0), dslots, dn,
-                                P.final_norm, nullptr, xq, fcol, scr);
+    // down_proj's partials (this GPU's slots, or every rank's, in rank order);
+    // under tensor parallelism gate|up's input also folds every rank's
+    // o_proj partial and keeps the sum as the mid residual
+    if (kind == DP_O || kind == DP_DOWN) {
+      dr_stage_plain<XP>(P, ph, target, kind == DP_O ? P.qdp : P.Fp, kind == DP_O ? P.qd : P.F,
+                         kind == DP_O ? P.ao : P.act, xq, fcol);
+    } else {
+      const int Lp = (kind == DP_LM ? P.L : L) - 1;  // layer of the down_proj folded in
+      const unsigned long long* xc = nullptr;
+      unsigned long long xt = 0;
+      const float* src = tp ? P.hm : ((Lp & 1) ? P.h1 : P.h0);
+      const float* slots = tp ? P.xin_me + dr_xin_region(Lp & 1, 1, P.tp, P.H) : P.pres;
+      int nsl = tp ? P.tp * P.nsf : P.nsf;
+      const uint16_t* nw = kind == DP_QKV ? ly->in_norm : (kind == DP_GU ? ly->post_norm : P.final_norm);
+      float* wb = kind == DP_QKV ? hc : nullptr;
+      if (tp && kind != DP_GU) {
+        xc = P.xcnt_me + 1;
+        xt = (s_epoch * (unsigned long long)P.L + (unsigned long long)Lp + 1) * (unsigned long long)P.gsum;
+      }
+      if (kind == DP_GU) {
+        src = hc;
+        if (tp) {
+          xc = P.xcnt_me + 0;
+          xt = (s_epoch * (unsigned long long)P.L + (unsigned long long)L + 1) * (unsigned long long)P.gsum;
+          slots = P.xin_me + dr_xin_region(L & 1, 0, P.tp, P.H);
+          nsl = P.tp;
+          wb = P.hm;
+        } else {
+          nsl = 0;
+        }
+      }
+      dr_stage_rms<XP>(P, ph, target, xc, xt, kind == DP_QKV && L == 0, src, slots, nsl, nw, wb, xq, fcol, scr);
     }
     float* red = reinterpret_cast<float*>(xq + (((size_t)d.K * 3 + 15) & ~(size_t)15));
+    const int n = d.s1 - d.s0;
+    const int t_lo = d.s0 / d.C;
+    const int ntile = n > 0 ? (d.s1 - 1) / d.C - t_lo + 1 : 0;
+    constexpr int NT = DR_CW * 32;
+    // o_proj adds into the residual: its rows (at most 16 tiles, one per
+    // thread) are read before the product so that the epilogue does not wait
+    float hres = 0.f;
+    if (!tp && kind == DP_O && threadIdx.x < ntile * 16) hres = __ldcg(hc + t_lo * 16 + threadIdx.x);
     dr_mark(P, ph, 1);
     dr_gemv_run(P, d, ring, full, empty, xq, fcol, red, u, warp, lane);
     dr_csync();
     dr_mark(P, ph, 2);
 
     // epilogue over the CTA's tiles
-    const int n = d.s1 - d.s0;
-    const int t_lo = d.s0 / d.C;
-    const int ntile = n > 0 ? (d.s1 - 1) / d.C - t_lo + 1 : 0;
-    constexpr int NT = DR_CW * 32;
     if (kind == DP_GU) {
       for (int i = threadIdx.x; i < ntile * 8; i += NT) {
         const int lt = i >> 3, r = i & 7;
@@ -1165,7 +1172,7 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P)
             for (int rk = 0; rk < DR_MAXTP; ++rk)
               if (rk < P.tp) P.xin[rk][off] = v;
           } else {
-            hc[row] = __ldcg(hc + row) + v;
+            hc[row] = (i == (int)threadIdx.x ? hres : __ldcg(hc + row)) + v;
           }
         } else {  // DP_DOWN: this CTA's partial of the tile into its slot;
                   // the tile's last CTA zeroes the slots no CTA fills
