@@ -670,7 +670,7 @@ __device__ __forceinline__ unsigned long long dr_key(float v, int idx) {
 template <int HD>
 __device__ void dr_attn(const DrParams& P, int L, uint8_t* ring, uint64_t* full, uint64_t* empty, int& u, float* sQ,
                         float* sP, float* sKn, float* sVn, float* sX, float (*sm_m)[DR_GMAX],
-                        float (*sm_l)[DR_GMAX], int* s_last, const float* sRope) {
+                        float (*sm_l)[DR_GMAX], int* s_last, const float* sRope, int ph) {
   constexpr int E = HD / 32, CH = HD / 4, J = HD / 32;
   const int c = blockIdx.x, ns = P.nsplit;
   if (c >= P.nkv * ns) return;
@@ -736,6 +736,7 @@ __device__ void dr_attn(const DrParams& P, int L, uint8_t* ring, uint64_t* full,
     dr_csync();
   }
 
+  dr_mark(P, ph, 1);  // prologue done
   float m[DR_GMAX], l[DR_GMAX], o[DR_GMAX][E];
 #pragma unroll
   for (int g = 0; g < DR_GMAX; ++g) {
@@ -848,6 +849,7 @@ __device__ void dr_attn(const DrParams& P, int L, uint8_t* ring, uint64_t* full,
   }
 #pragma unroll
   for (int g = 0; g < DR_GMAX; ++g) l[g] = warp_sum(l[g]);
+  dr_mark(P, ph, 2);  // this warp's blocks done (marks come from warp 0)
 
   // merge the consumer warps: (m, l, o) per head, o staged in sX
   float* sO = sX;  // [DR_CW][DR_GMAX][HD]
@@ -1032,9 +1034,7 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P)
       dr_grid_wait(P, target);
       dr_mark(P, ph, 0);
       dr_attn<HD>(P, L, ring, full, empty, u, sQ, sP, sKn, sVn, reinterpret_cast<float*>(xq), sm_m, sm_l, &s_last,
-                  s_rope);
-      dr_mark(P, ph, 1);
-      dr_mark(P, ph, 2);
+                  s_rope, ph);
       dr_grid_arrive(P);
       dr_mark(P, ph, 3);
       continue;
@@ -1042,7 +1042,6 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P)
     const DrG d = dr_gemv_desc(P, kind, L);
     const DrLayer* ly = P.layers + (kind == DP_LM ? 0 : L);
     float* hc = (L & 1) ? P.h1 : P.h0;  // this layer's residual
-    float* hp = (L & 1) ? P.h0 : P.h1;  // the previous layer's
     // the stagings wait for the previous phase (after their static loads);
     // mark 0 is then the end of the wait.  Folds: the residual + the previous
     // down_proj's partials (this GPU's slots, or every rank's, in rank order);
