@@ -311,6 +311,8 @@ __global__ void __launch_bounds__(AD_THREADS, 1) k_attn_dec(AdArgs a, const __gr
         *reinterpret_cast<float4*>(kb + ad_kofs<HD, TM>(p - key0, c)) = *reinterpret_cast<const float4*>(sKn + 4 * c);
         *reinterpret_cast<float4*>(vb + (p - key0) * HD + 4 * c) = *reinterpret_cast<const float4*>(sVn + 4 * c);
       }
+      // generic writes land before the bulk copies that later refill the slot
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
     }
 

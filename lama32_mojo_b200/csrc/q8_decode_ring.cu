@@ -249,7 +249,7 @@ __device__ __forceinline__ DrG dr_gemv_desc(const DrParams& P, int kind, int L) 
     case DP_QKV: d.W = ly->qkv; d.K = P.H; N = P.nqkv; break;
     case DP_O: d.W = ly->o; d.K = P.qdp; N = P.H; break;
     case DP_GU: d.W = ly->gu; d.K = P.H; N = P.F; d.F2 = P.F; break;
-    case DP_DOWN: d.W = ly->down; d.K = P.Fp; N = P.H; d.split = 1; break;
+    case DP_DOWN: d.W = ly->down; d.K = P.Fp; N = P.H; d.split = dr_down_split(P.Fp); break;
     default: d.W = P.lm_head; d.K = P.H; N = P.V; break;
   }
   d.T = d.F2 ? N / 8 : N / 16;
@@ -665,6 +665,9 @@ __device__ __forceinline__ unsigned long long dr_key(float v, int idx) {
   return ((unsigned long long)b << 32) | (uint32_t)(~(uint32_t)idx);
 }
 
+// splits whose partials one thread of the merging CTA has in flight together
+constexpr int DR_MRG = 10;
+
 // ------------------------------------------------------------------ attention consumer
 
 template <int HD>
@@ -921,11 +924,11 @@ __device__ void dr_attn(const DrParams& P, int L, uint8_t* ring, uint64_t* full,
     const int r0 = run * ns / nrun, r1 = (run + 1) * ns / nrun;
     float M = -INFINITY, Ls = 0.f;
     float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s0 = r0; s0 < r1; s0 += 8) {
-      float4 v[8];
-      float ms[8], ls[8];
+    for (int s0 = r0; s0 < r1; s0 += DR_MRG) {
+      float4 v[DR_MRG];
+      float ms[DR_MRG], ls[DR_MRG];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
+      for (int q = 0; q < DR_MRG; ++q) {
         const bool ok = s0 + q < r1;
         const float* ps = base + (int64_t)(s0 + q) * WS;
         v[q] = ok ? __ldcg(reinterpret_cast<const float4*>(ps) + i4) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -933,7 +936,7 @@ __device__ void dr_attn(const DrParams& P, int L, uint8_t* ring, uint64_t* full,
         ls[q] = ok ? __ldcg(ps + G * HD + G + g) : 0.f;
       }
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
+      for (int q = 0; q < DR_MRG; ++q) {
         if (ms[q] == -INFINITY) continue;
         const float mn = fmaxf(M, ms[q]);
         const float cf = exp2f(M - mn), f = exp2f(ms[q] - mn);
@@ -1176,8 +1179,8 @@ __global__ void __launch_bounds__(DR_THREADS, 1) k_decode_ring(const DrParams P)
         } else {  // DP_DOWN: this CTA's partial of the tile into its slot;
                   // the tile's last CTA zeroes the slots no CTA fills
           const long long S = (long long)d.T * d.C;
-          const int c0 = dr_cta_of((long long)tile * d.C, S, d.C);
-          const int c1 = dr_cta_of((long long)(tile + 1) * d.C - 1, S, d.C);
+          const int c0 = d.split ? dr_cta_of((long long)tile * d.C, S, d.C) : c;
+          const int c1 = d.split ? dr_cta_of((long long)(tile + 1) * d.C - 1, S, d.C) : c;
           if (tp) {
             const int64_t base = dr_xin_region(L & 1, 1, P.tp, P.H) + (int64_t)P.rank * P.nsf * P.H + row;
 #pragma unroll
@@ -1277,13 +1280,20 @@ size_t dr_apart_floats(int nkv, int nsplit, int hd) {
 // Partial slots per down-projection tile: a tile of C stages meets at most
 // ceil((C - 1) / per) + 1 of the split ranges (each >= per stages).
 int dr_down_nsf(int H, int F, int G) {
+  if (!dr_down_split(F)) return 1;
   const int C = F / DR_CK;
   const long long S = (long long)(H / 16) * C;
   const long long per = S / dr_split_ctas(S, C, G);
   return (int)((C - 2 + per) / per + 1);
 }
 
-int dr_nsplit(int G, int nkv) { return std::max(1, std::min(DR_MAXSPLIT, G / std::max(1, nkv))); }
+// Context splits per kv head: enough CTAs to cover the SMs, but no more than
+// give each split one 16-position block per consumer warp at the longest
+// context (more splits only lengthen the merge, which every layer waits for).
+int dr_nsplit(int G, int nkv, int maxlen) {
+  const int by_ctx = ((maxlen + 15) / 16 + DR_CW - 1) / DR_CW;
+  return std::max(1, std::min({DR_MAXSPLIT, G / std::max(1, nkv), by_ctx}));
+}
 
 bool dr_supported(int H, int nh, int nkv, int hd, int F, int V, int page, const char** why) {
   auto no = [&](const char* w) {

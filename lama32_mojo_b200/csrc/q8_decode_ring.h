@@ -114,7 +114,11 @@ bool dr_supported(int H, int nh, int nkv, int hd, int F, int V, int page, const 
 inline int dr_kpad(int K) { return (K + DR_CK - 1) / DR_CK * DR_CK; }
 int dr_prepare(int hd, int* grid);  // kernel attributes, residency check; grid = CTAs (one per SM)
 size_t dr_apart_floats(int nkv, int nsplit, int hd);
-int dr_nsplit(int G, int nkv);
+int dr_nsplit(int G, int nkv, int maxlen);
+// down_proj tiles are split over CTAs (partial rows into slots) when they are
+// at least 8 chunks deep; shallower ones (tensor-parallel slices) stay whole,
+// so that each rank sends one partial row per output
+__host__ __device__ inline bool dr_down_split(int Fp) { return Fp / DR_CK >= 8; }
 int dr_down_nsf(int H, int F, int G);
 int dr_launch(const DrParams& p, int grid, cudaStream_t st);
 // Copies a packed-row matrix (rows x K, SwiGLU: 2 F rows with f2 = F) into

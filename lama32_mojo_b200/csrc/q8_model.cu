@@ -1097,7 +1097,7 @@ static int create_impl(const q8_config* cfg, int device, int max_seqs, int maxle
     }
     if (c->dr_grid > 0) {
       const int nqkv = c->qd + 2 * c->kvd;
-      c->dr_nsplit = dr_nsplit(c->dr_grid, c->nkv);
+      c->dr_nsplit = dr_nsplit(c->dr_grid, c->nkv, maxlen);
       if ((s = dmalloc((void**)&c->dr_h1, (size_t)H * 4))) return bail(s);
       if ((s = dmalloc((void**)&c->dr_pres, (size_t)DR_NS * H * 4))) return bail(s);
       if ((s = dmalloc((void**)&c->dr_apart, dr_apart_floats(c->nkv, c->dr_nsplit, c->hd) * 4))) return bail(s);

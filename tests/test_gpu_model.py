@@ -305,14 +305,16 @@ def test_ring_decode_step_matches_per_op(cuda, cfgname, monkeypatch):
     checkpoint: cached decode logits match the oracle and each other, and
     on-device generation, per-step decode and batched decode give the same
     tokens.  The context grows past several 16-position blocks so that the
-    attention splits and the KV append of the ring step are exercised."""
+    KV append of the ring step is exercised, and the capacity (1024) gives
+    the attention 8 context splits per kv head, most of them empty, so that
+    the split merge is exercised."""
     ocfg = O.PRESETS[cfgname]
     ck = O.make_q8_checkpoint(ocfg)
     ids = O.random_ids(ocfg, 45, seed=21)
     out = {}
     for ring in ("0", "1"):
         monkeypatch.setenv("Q8_RING", ring)
-        m = build(cfgname, maxlen=96, max_seqs=2)
+        m = build(cfgname, maxlen=1024, max_seqs=2)
         m.set_profiling(True)
         m.forward(ids[:-1])
         lg = m.forward([ids[-1]])
