@@ -46,9 +46,22 @@ def test_status_codes_match_header():
 
 def test_config_struct_layout():
     import ctypes as C
-    # int32 x7 + float (32 B), double x5 (40 B), int32 x3 + tail pad (16 B) on x86-64
+    # int32 x7 + float (32 B), double x5 (40 B), int32 x4 (16 B) on x86-64
     assert C.sizeof(_lib.q8_config) == 88
     assert _lib.q8_config.theta.offset == 32 and _lib.q8_config.rope_type.offset == 72
+    assert _lib.q8_config.weight_dtype.offset == 84
+
+
+def test_config_weight_dtype_to_c():
+    """The bf16 shells' configs select bf16 weights; everything else packed Q8."""
+    from lama32_mojo_b200 import PRESETS
+    cfg = PRESETS["tiny-llama"]
+    assert cfg.to_c().weight_dtype == _lib.Q8_PACKED
+    assert cfg.replace(weights="bf16").to_c().weight_dtype == _lib.Q8_BF16
+    # decode bytes count 2-byte weights for bf16, 33/32 bytes for Q8
+    w8 = cfg.decode_bytes(1, 0)
+    w16 = cfg.replace(weights="bf16").decode_bytes(1, 0)
+    assert abs(w16 / w8 - 2.0 / (1 + 2 / 64)) < 1e-9
 
 
 @pytest.mark.parametrize("name", ["llama-3.2-1b", "llama-3.1-8b", "qwen3-8b", "tiny-llama"])
