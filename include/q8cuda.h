@@ -219,7 +219,13 @@ int q8op_sample(const float* logits, int64_t rows, int64_t n, int64_t ld, float 
  *   maxlen    KV capacity per sequence (reference `maxlen`)
  *   max_tokens  largest token batch one forward processes (prefill is chunked)
  *   tp_rank/tp_size  tensor-parallel position (1 = single GPU)
- *   nccl_id   128-byte ncclUniqueId from q8_nccl_unique_id() (NULL if tp_size==1) */
+ *   nccl_id   128-byte ncclUniqueId from q8_nccl_unique_id() (NULL if tp_size==1)
+ * Collective when tp_size > 1: every rank calls it.  The ranks map each
+ * other's exchange buffers (CUDA IPC) and agree on whether one-sequence greedy
+ * decode steps run as one launch with the row-parallel sums exchanged inside
+ * it (every rank or none).  After a model call returned Q8_ERR_COMM or
+ * Q8_ERR_TIMEOUT the ranks' exchange state no longer agrees: destroy and
+ * recreate the contexts. */
 int q8_create(const q8_config* cfg, int device, int max_seqs, int maxlen, int max_tokens,
               int tp_rank, int tp_size, const void* nccl_id, q8_ctx** out);
 int q8_destroy(q8_ctx* ctx);
